@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized-linear hot path on B200.
+
+Workload: the FLUX.1-dev-shaped Q8 double-stream block
+linears, group 64, bf16, batch 1, M = 4608 tokens:
+    QKV 3072->9216 (+bias), attn-out 3072->3072 (+bias),
+    MLP up 3072->12288 (+bias, GELU-tanh fused), MLP down 12288->3072 (+bias)
+One step = those four quantized_matmul calls (the down projection consumes the up
+projection's output) = 1043.7 GFLOP.  Weights ~N(0, 0.02) quantized on the device,
+activations ~N(0, 1), seeded synthetic data (no checkpoint or dataset involved).
+Each step touches ~300 MB (> the 126 MB L2), so no explicit L2 flush is needed.
+
+N > 1 GPUs (torchrun, one rank per GPU, NCCL): Megatron tensor parallelism of the same
+block -- QKV / up column-parallel, out / down row-parallel with one all-reduce each --
+so total work is fixed ("scaling": "strong").
+
+Also reported (rank 0, N = 1):
+  * "roofline": the tcgen05 GEMM kernel's achieved TFLOP/s (algorithmic 2*M*N*K per
+    launch / CUDA-event launch time) against the measured bf16 peak;
+  * "e2e": the same metric through the public API with host buffers (pinned H2D of x,
+    D2H of the block output inside the timed region);
+  * "cpu_baseline": the CPU oracle (oracle/qref.c, fast mode, all host threads) on a
+    bounded sample of the workload;
+  * "decode_gemv": the Llama-3.2-3B Q4 decode step at M = 1 in HBM GB/s.
+
+`--impl reference` times the reference path's CPU implementation instead (the oracle
+restatement of MLX's affine quantized_matmul; MLX itself cannot be built here).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mlx-gen_b200"))
+
+FLUX = dict(M=4608, hidden=3072, mlp=12288, bits=8, gs=64)
+METRIC = "quantized_matmul TFLOP/s (DiT M) and HBM GB/s (M=1) vs B200 peak"
+
+
+def flux_linears(cfg):
+    h, f = cfg["hidden"], cfg["mlp"]
+    # name, N, K, act, parallel style
+    return [("qkv", 3 * h, h, None, "col"), ("out", h, h, None, "row"),
+            ("up", f, h, "gelu_tanh", "col"), ("down", h, f, None, "row")]
+
+
+def flux_flops(cfg):
+    return sum(2.0 * cfg["M"] * N * K for _, N, K, _, _ in flux_linears(cfg))
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200", "-i", str(gpu_index)], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.seek(0)
+        rows = [r.split(", ") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------- reference arm
+
+def run_reference(args):
+    """Times the CPU implementation of the path (oracle fast mode) on a bounded sample."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O  # CPU restatement of MLX's affine quantized_matmul
+
+    cfg = dict(FLUX)
+    Ms = 32  # bounded sample: 32 of the 4608 tokens per step
+    rng = np.random.default_rng(0)
+    lin = []
+    for name, N, K, act, _ in flux_linears(cfg):
+        w = O.to_bf16((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+        wq, s, b = O.quantize(w, cfg["gs"], cfg["bits"])
+        lin.append((name, wq, s, b, O.to_bf16((rng.standard_normal(N) * 0.02).astype(np.float32))))
+    x = O.to_bf16(rng.standard_normal((Ms, cfg["hidden"])).astype(np.float32))
+    u_in = O.to_bf16(rng.standard_normal((Ms, cfg["mlp"])).astype(np.float32))
+    threads = os.cpu_count() or 1
+
+    def step():
+        for name, wq, s, b, bias in lin:
+            O.quantized_matmul_fast(u_in if name == "down" else x, wq, s, b, cfg["gs"], cfg["bits"], bias=bias,
+                                    threads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    flops = flux_flops(dict(cfg, M=Ms))
+    v = flops / dt / 1e12
+    out = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+           "config": {"workload": "flux_q8_block_linears", "M": cfg["M"], "sample_tokens": Ms, "bits": 8,
+                      "group_size": 64},
+           "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                            "sample": f"{Ms} of {cfg['M']} tokens through the 4 FLUX block linears per step"},
+           "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "note": "MLX (the reference's backend) cannot be built here; this is the CPU oracle "
+                   "restatement (oracle/qref.c) pinned to the reference fixture"}
+    print(json.dumps(out), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+def cpu_baseline_sample(cfg):
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    Ms = 32
+    rng = np.random.default_rng(1)
+    threads = os.cpu_count() or 1
+    t_total, flops = 0.0, 0.0
+    for name, N, K, act, _ in flux_linears(cfg):
+        w = O.to_bf16((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+        wq, s, b = O.quantize(w, cfg["gs"], cfg["bits"])
+        x = O.to_bf16(rng.standard_normal((Ms, K)).astype(np.float32))
+        O.quantized_matmul_fast(x, wq, s, b, cfg["gs"], cfg["bits"], threads=threads)  # warm
+        t0 = time.perf_counter()
+        O.quantized_matmul_fast(x, wq, s, b, cfg["gs"], cfg["bits"], threads=threads)
+        t_total += time.perf_counter() - t0
+        flops += 2.0 * Ms * N * K
+    return {"value": flops / t_total / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{Ms} of {cfg['M']} tokens through the 4 FLUX block linears (oracle fast mode)"}
+
+
+def decode_gemv(dev, steps=20, warmup=5):
+    """Llama-3.2-3B Q4 g64 decode step at M=1: 28 x (qkv, o, gate/up SwiGLU, down) + lm_head."""
+    import torch
+    import qlinear
+
+    H, I, V, L, KV = 3072, 8192, 128256, 28, 1024
+    g = torch.Generator(device=dev).manual_seed(3)
+
+    def qlin(N, K):
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        return qlinear.quantize(w, 64, 4)
+
+    layers = []
+    for _ in range(L):
+        layers.append(dict(qkv=qlin(H + 2 * KV, H), o=qlin(H, H), gate=qlin(I, H), up=qlin(I, H), down=qlin(H, I)))
+    head = qlin(V, H)
+    h = torch.randn(1, H, device=dev, generator=g).to(torch.bfloat16)
+    bufs = dict(qkv=torch.empty(1, H + 2 * KV, device=dev, dtype=torch.bfloat16),
+                o=torch.empty(1, H, device=dev, dtype=torch.bfloat16),
+                g=torch.empty(1, I, device=dev, dtype=torch.bfloat16),
+                h=torch.empty(1, H, device=dev, dtype=torch.bfloat16),
+                logits=torch.empty(1, V, device=dev, dtype=torch.bfloat16))
+
+    def step():
+        x = h
+        for ly in layers:
+            qlinear.quantized_matmul(x, *ly["qkv"], True, 64, 4, out=bufs["qkv"])
+            qlinear.quantized_matmul(x, *ly["o"], True, 64, 4, out=bufs["o"])
+            qlinear.quantized_matmul(bufs["o"], *ly["gate"], True, 64, 4, act="swiglu", up=ly["up"], out=bufs["g"])
+            qlinear.quantized_matmul(bufs["g"], *ly["down"], True, 64, 4, out=bufs["h"])
+            x = bufs["h"]
+        qlinear.quantized_matmul(x, *head, True, 64, 4, out=bufs["logits"])
+
+    def nbytes(N, K):
+        return N * K * 4 // 8 + N * (K // 64) * 4 + (K + N) * 2
+
+    per_layer = nbytes(H + 2 * KV, H) + nbytes(H, H) + 2 * nbytes(I, H) - (H * 2) + nbytes(H, I)
+    total_bytes = L * per_layer + nbytes(V, H)
+    step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        step()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=s):
+            step()
+    torch.cuda.synchronize()
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"workload": "llama3.2-3b_q4_g64_decode_M1", "value": total_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
+            "ms_per_step": ms, "bytes_per_step": total_bytes, "launches_per_step": 4 * L + 1,
+            "timing": "CUDA graph of one decode step; 1.8 GB of weights per step (> L2)"}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import qlinear
+    from qlinear import tp
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    cfg = dict(FLUX)
+    M, gs, bits = cfg["M"], cfg["gs"], cfg["bits"]
+
+    # weights: generated and quantized identically on every rank, then sharded
+    g = torch.Generator(device=dev).manual_seed(0)
+    lin = {}
+    for name, N, K, act, style in flux_linears(cfg):
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        bias = (torch.randn(N, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        wq, s, b = qlinear.quantize(w, gs, bits)
+        del w
+        if world > 1 and style == "col":
+            wq, s, b, bias = tp.column_shard(wq, s, b, bias, rank, world)
+        elif world > 1 and style == "row":
+            wq, s, b, _, _ = tp.row_shard(wq, s, b, gs, bits, rank, world)
+            if rank != 0:
+                bias = None  # added once: the all-reduce sums rank 0's biased partial
+        lin[name] = dict(wq=wq, s=s, b=b, bias=bias, act=act, style=style, N=s.shape[0], K=s.shape[1] * gs)
+    x = torch.randn(M, cfg["hidden"], device=dev, generator=g).to(torch.bfloat16)
+    out = {n: torch.empty(M, l["N"], device=dev, dtype=torch.bfloat16) for n, l in lin.items()}
+    torch.cuda.synchronize()
+
+    evs = []  # (name, start, end) of every GEMM launch in the timed region
+
+    def step(record=False, xin=None):
+        xin = x if xin is None else xin
+        for name in ("qkv", "out", "up", "down"):
+            l = lin[name]
+            inp = out["up"] if name == "down" else xin
+            if record:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+            qlinear.quantized_matmul(inp, l["wq"], l["s"], l["b"], True, gs, bits, bias=l["bias"], act=l["act"],
+                                     kernel=qlinear.KERNEL_GEMM, out=out[name])
+            if record:
+                e1.record()
+                evs.append((name, e0, e1))
+            if world > 1 and l["style"] == "row":
+                dist.all_reduce(out[name])
+        return out["down"]
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local) if rank == 0 else None
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step(record=(world == 1))
+    t1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+    ck = clocks.stop() if clocks else None
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    total_flops = flux_flops(cfg)
+    value = total_flops / (ms * 1e-3) / 1e12
+    assert qlinear.device_error() == 0, "a kernel reported a device-side error"
+
+    result = None
+    if rank == 0:
+        peaks, src = load_peaks()
+        result = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+                  "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+                  "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                  "data": "synthetic (seeded; W~N(0,0.02) quantized Q8 g64 on device, x~N(0,1))",
+                  "config": {"workload": "flux_q8_block_linears", "M": M, "hidden": cfg["hidden"],
+                             "mlp": cfg["mlp"], "bits": bits, "group_size": gs,
+                             "flops_per_step": total_flops,
+                             "parallelism": f"tp{world}" if world > 1 else "single",
+                             "l2": "no flush: each step touches ~300 MB (> 126 MB L2)"},
+                  "gpu_launches": 4 * args.steps + (0 if world == 1 else 0),
+                  "clocks": ck}
+        if world == 1:
+            # roofline of the dominant kernel (qgemm_sm100): algorithmic flops / event time per launch
+            per = {}
+            for name, e0, e1 in evs:
+                per.setdefault(name, []).append(e0.elapsed_time(e1))
+            k_ms = sum(statistics.mean(v) for v in per.values())
+            achieved = total_flops / (k_ms * 1e-3) / 1e12
+            peak = peaks["bf16_tflops_sustained"]
+            result["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                                  "frac": achieved / peak, "peak_kind": f"{src} bf16 sustained",
+                                  "frac_of_burst": achieved / peaks["bf16_tflops"],
+                                  "traffic": None, "kernel": "qgemm_sm100 (4 launches/step, mean ms each)",
+                                  "per_launch_ms": {k: statistics.mean(v) for k, v in per.items()}}
+    # e2e through the public API with host buffers
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(M, cfg["hidden"], dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(args.steps):
+        xd.copy_(xh, non_blocking=True)
+        y = step(xin=xd)
+        yh.copy_(y, non_blocking=True)
+    t1.record()
+    torch.cuda.synchronize()
+    e2e_ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    if rank == 0:
+        result["e2e"] = {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                         "h2d_bytes_per_step": xh.numel() * 2, "d2h_bytes_per_step": yh.numel() * 2,
+                         "ms_per_step": e2e_ms}
+        if world == 1 and not args.no_extras:
+            result["cpu_baseline"] = cpu_baseline_sample(cfg)
+            result["decode_gemv"] = decode_gemv(dev)
+            peaks, src = load_peaks()
+            result["decode_gemv"]["frac_of_hbm"] = result["decode_gemv"]["value"] / peaks["hbm_gbs"]
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-extras", action="store_true", help="skip cpu_baseline and decode_gemv")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

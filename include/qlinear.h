@@ -1,0 +1,135 @@
+/*
+ * qlinear.h -- C ABI of libqlinear, the B200 (sm_100a) group-wise affine Q4/Q8
+ * quantized-linear library.
+ *
+ * This ABI is the drop-in boundary for the reference's quantized-linear path.
+ * The reference (SceneWorks/mlx-gen, Rust on MLX) reaches the arithmetic
+ * through mlx-rs; each entry point below names the call it replaces.
+ *
+ * Conventions
+ *   - Every pointer argument is caller-owned DEVICE memory (except ql_last_error's
+ *     result).  The library allocates nothing on any call path.
+ *   - Row-major, contiguous.  W is [N, K] (out, in), x is [M, K], y is [M, N].
+ *   - Packing (byte-identical to MLX affine quantization): wq is uint32
+ *     [N, K*bits/32]; element k of a row is code (wq[k/(32/bits)] >> (bits*(k%(32/bits))))
+ *     & (2^bits-1); scales / biases are [N, K/group_size]; w = code*scale + bias.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are
+ *     asynchronous, hold no global mutable state and may run concurrently on
+ *     different streams.
+ *   - Return value is a ql_status.  On failure, ql_last_error() returns a
+ *     thread-local message.  No call aborts or exits.
+ */
+#ifndef QLINEAR_H
+#define QLINEAR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    QL_F32 = 0,
+    QL_BF16 = 1,
+    QL_F16 = 2,
+} ql_dtype;
+
+typedef enum {
+    QL_OK = 0,
+    QL_EINVAL_SHAPE = 1,  /* K % group_size, sizes <= 0, mismatched shapes      */
+    QL_EUNSUPPORTED = 2,  /* bits not in {4,8}, group_size not in {32,64,128},
+                             dtype combination without a kernel                 */
+    QL_ECUDA = 3,         /* a CUDA runtime / driver call failed                */
+    QL_EINVAL_ARG = 4,    /* NULL pointer, misaligned pointer, small workspace  */
+    QL_ETIMEOUT = 5,      /* a kernel's bounded wait ran out (see ql_device_error) */
+} ql_status;
+
+typedef enum {
+    QL_ACT_NONE = 0,
+    QL_ACT_GELU_TANH = 1, /* 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))     */
+    QL_ACT_GELU_ERF = 2,  /* 0.5 x (1 + erf(x / sqrt 2))                         */
+    QL_ACT_SWIGLU = 3,    /* silu(x W^T) * (x W_up^T); needs the *_up weights    */
+} ql_act;
+
+typedef enum {
+    QL_KERNEL_AUTO = 0,    /* GEMV for M <= 8, tcgen05 GEMM otherwise (bf16)    */
+    QL_KERNEL_GENERIC = 1, /* CUDA-core fp32 kernel; any dtype                   */
+    QL_KERNEL_GEMV = 2,    /* M <= 8, bf16 x and bf16 scales                     */
+    QL_KERNEL_GEMM = 3,    /* tcgen05 / TMEM GEMM, bf16 x and bf16 scales        */
+} ql_kernel;
+
+/* Fused epilogue and options of ql_quantized_matmul.  Zero-initialise, then set
+ * what is needed.  Replaces the ops the reference runs after quantized_matmul:
+ * the bias add (src/adapters.rs:318-320), the LoRA residual sum
+ * (src/adapters.rs:260-270,545-547), GELU (src/nn.rs:321-355) and SwiGLU
+ * (mlx-gen-z-image/src/feed_forward.rs:34-38). */
+typedef struct {
+    const void *bias;          /* [N] in y's dtype, or NULL                           */
+    int act;                   /* ql_act                                               */
+    /* SwiGLU second projection (w3 / "up"), same shapes and dtypes as the main one. */
+    const uint32_t *wq_up;
+    const void *scales_up;
+    const void *biases_up;
+    const void *bias_up;       /* [N] or NULL                                          */
+    /* LoRA residual: y += lora_scale * (x . A) . B with A [K, rank], B [rank, N] in
+     * x's dtype.  rank % 8 == 0.  Needs `workspace` of ql_matmul_workspace_size(). */
+    const void *lora_a;
+    const void *lora_b;
+    int64_t lora_rank;
+    float lora_scale;
+    void *workspace;
+    size_t workspace_bytes;
+    int kernel;                /* ql_kernel (QL_KERNEL_AUTO unless testing a path)     */
+} ql_epilogue;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int ql_version(void);
+
+/* Thread-local message describing the last failure on this thread ("" if none). */
+const char *ql_last_error(void);
+
+/* Reads (and with clear != 0 resets) the device-side error word that kernels set
+ * when a bounded wait runs out.  Synchronises the current device.  0 = no error. */
+int ql_device_error(int clear);
+
+/* Replaces mlx_rs::ops::quantize(w, group_size, bits) -> (wq, scales, biases)
+ * (called at src/quant.rs:140, src/adapters.rs:533-537 via
+ * QuantizedLinear::try_from_linear, src/nn.rs:91-93).  w [N, K] in w_dtype;
+ * scales/biases written in sb_dtype (the reference stores them in w's dtype). */
+int ql_quantize(const void *w, int w_dtype, int64_t N, int64_t K, int group_size, int bits,
+                uint32_t *wq, void *scales, void *biases, int sb_dtype, void *stream);
+
+/* Replaces mlx_rs::ops::dequantize(wq, scales, biases, group_size, bits)
+ * (src/nn.rs:55, tests/quant_parity.rs:53).  out [N, K] in out_dtype;
+ * w = fma(code, scale, bias) in fp32, rounded once. */
+int ql_dequantize(const uint32_t *wq, const void *scales, const void *biases, int sb_dtype,
+                  int64_t N, int64_t K, int group_size, int bits, void *out, int out_dtype,
+                  void *stream);
+
+/* Replaces the quantized TokenEmbedding gather: take_axis(wq|scales|biases, ids)
+ * followed by dequantize and a cast (src/nn.rs:42-59).  ids [R] int64 into the
+ * N rows; out [R, K] in out_dtype.  An id outside [0, N) yields a zero row and
+ * sets the device error word. */
+int ql_dequantize_rows(const int64_t *ids, int64_t R, const uint32_t *wq, const void *scales,
+                       const void *biases, int sb_dtype, int64_t N, int64_t K, int group_size,
+                       int bits, void *out, int out_dtype, void *stream);
+
+/* Replaces mlx_rs::ops::quantized_matmul(x, wq, scales, biases, transpose=true,
+ * group_size, bits) as called by LinearBase::forward (src/adapters.rs:309-317),
+ * plus the ops fused through `ep` (may be NULL).  y [M, N] in y_dtype.
+ * transpose must be 1 (the only form the reference uses). */
+int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const uint32_t *wq,
+                        const void *scales, const void *biases, int sb_dtype, int64_t N,
+                        int group_size, int bits, int transpose, const ql_epilogue *ep,
+                        void *y, int y_dtype, void *stream);
+
+/* Bytes of device workspace ql_quantized_matmul needs for this shape and
+ * epilogue (0 when none; the LoRA residual needs M * round_up(rank, 64) * 2). */
+size_t ql_matmul_workspace_size(int64_t M, int64_t N, int64_t K, const ql_epilogue *ep);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QLINEAR_H */

@@ -1,0 +1,501 @@
+// qgemm_sm100.cu -- large-M quantized GEMM on tcgen05 tensor cores (sm_100a).
+//
+// Computes y[M, N] = x[M, K] . dequant(W)[N, K]^T (+ LoRA residual) with a
+// fused bias / GELU / SwiGLU epilogue.  This replaces MLX's quantized_matmul as
+// called by LinearBase::forward (src/adapters.rs:309-320) for bf16 activations.
+//
+// Design (B200-first, not a translation of any reference kernel):
+//   * The MMA is transposed: D^T = W_tile . x_tile^T.  The 128 weight rows of a
+//     tile are the MMA's M side and live in TENSOR MEMORY as the A operand; the
+//     256 tokens of the tile are the N side and stream through shared memory.
+//     Dequantized weights therefore never round-trip through shared memory:
+//     packed words arrive by TMA, dequant warps turn them into bf16 in
+//     registers and write them straight into TMEM with tcgen05.st.  Shared
+//     memory bandwidth is spent only on the x tiles the MMA reads.
+//   * Warp roles in a 512-thread CTA (one CTA per SM, persistent over tiles):
+//       warp 0      TMA producer (x tile + packed W tile per k-step)
+//       warp 1      TMEM allocator and single-thread tcgen05.mma issuer
+//       warps 4-7   epilogue (TMEM -> registers -> bias/act -> global)
+//       warps 8-15  two dequant warpgroups, alternating k-steps
+//   * Pipelines: STAGES-deep smem ring (x + packed W) and a 4-slot TMEM ring of
+//     dequantized A tiles, each guarded by full/empty mbarriers.  The fp32
+//     accumulator (128 lanes x 256 columns) occupies TMEM columns [0, 256).
+//   * LoRA: the residual s.(x.A).B is folded into the same accumulator as extra
+//     k-steps: T = s.(x.A) (a small pre-pass, [M, r_pad] bf16) is the smem
+//     operand and B^T (rows of B for this tile) is written to TMEM as A.
+//   * SwiGLU: a tile holds 64 rows of W1 (gate) in TMEM lanes 0-63 and the same
+//     64 rows of W3 (up) in lanes 64-127; the epilogue pairs them through smem.
+//   * Every mbarrier wait is bounded (ql_common.cuh mbar_wait); on timeout the
+//     kernel records an error, every role drains, and TMEM is freed.
+#include "ql_common.cuh"
+
+namespace ql {
+
+namespace gemm {
+
+constexpr int BT = 256;        // tokens per tile (MMA N)
+constexpr int BW = 128;        // weight rows per tile (MMA M)
+constexpr int BK = 64;         // K per pipeline step (one 128-byte swizzle row of bf16)
+constexpr int STAGES = 5;      // smem ring depth
+constexpr int AST = 4;         // TMEM A ring depth (32 columns each)
+constexpr int NTHREADS = 512;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t ACC_COL = 0;
+constexpr uint32_t A_COL = 256;
+constexpr int X_STAGE_BYTES = BT * BK * 2;  // 32 KB
+
+template <int BITS>
+struct Cfg {
+    static constexpr int W_ROW_BYTES = BK * BITS / 8;           // 32 (Q4) / 64 (Q8)
+    static constexpr int W_STAGE_BYTES = BW * W_ROW_BYTES;      // 4 KB / 8 KB
+    static constexpr int W_BOX_WORDS = BK * BITS / 32;          // 8 / 16
+    static constexpr int SMEM_X = 0;
+    static constexpr int SMEM_W = SMEM_X + STAGES * X_STAGE_BYTES;
+    static constexpr int SMEM_XCH = SMEM_W + STAGES * W_STAGE_BYTES;  // swiglu exchange
+    static constexpr int XCH_BYTES = 64 * 33 * 4;
+    static constexpr int SMEM_BAR = SMEM_XCH + XCH_BYTES;
+    static constexpr int NBAR = 2 * STAGES + 2 * AST + 2;
+    static constexpr int SMEM_MISC = SMEM_BAR + NBAR * 8;
+    static constexpr int SMEM_TOTAL = SMEM_MISC + 16 + 1024;  // + alignment slack
+};
+
+struct Params {
+    int M, N, K;            // N: output columns (for SwiGLU, rows of W1 == rows of W3)
+    int gs, G;              // group size, groups per row
+    int ktw;                // k-steps over W (ceil(K / BK))
+    int ktl;                // LoRA k-steps (ceil(rank_pad / BK)), 0 if none
+    int act;
+    int num_w_tiles, num_t_tiles;
+    const __nv_bfloat16 *scales, *biases;
+    const __nv_bfloat16 *scales2, *biases2;  // SwiGLU up projection
+    const __nv_bfloat16 *bias, *bias2;
+    const __nv_bfloat16 *lora_b;             // [rank, N]
+    int lora_rank;
+    __nv_bfloat16 *y;
+};
+
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+    const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+    float t;
+    const float inner = k0 * (x + k1 * x * x * x);
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(inner));
+    return 0.5f * x * (1.0f + t);
+}
+
+__device__ __forceinline__ float gelu_erf_f(float x) {
+    return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f));
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+// Epilogue value for one output: the reference rounds the matmul to the output
+// dtype, then adds the bias as a separate bf16 op (src/adapters.rs:318-320),
+// then applies the activation.
+__device__ __forceinline__ float epi_value(float acc, float bias, bool has_bias, int act) {
+    float v = round_bf16(acc);
+    if (has_bias) v = round_bf16(v + bias);
+    if (act == QL_ACT_GELU_TANH) v = gelu_tanh_f(v);
+    else if (act == QL_ACT_GELU_ERF) v = gelu_erf_f(v);
+    return v;
+}
+
+template <int BITS, bool SWIGLU>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    qgemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                 const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_t,
+                 const Params p) {
+    using C = Cfg<BITS>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::SMEM_BAR);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + STAGES;
+    uint64_t *afull = bars + 2 * STAGES;
+    uint64_t *aempty = afull + AST;
+    uint64_t *accfull = aempty + AST;
+    uint64_t *accempty = accfull + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::SMEM_MISC);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::SMEM_MISC + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_tiles = p.num_w_tiles * p.num_t_tiles;
+    const int KT = p.ktw + p.ktl;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1 + 4);  // MMA commit + 4 dequant warps
+        }
+        for (int j = 0; j < AST; ++j) {
+            mbar_init(&afull[j], 4);
+            mbar_init(&aempty[j], 1);
+        }
+        mbar_init(accfull, 1);
+        mbar_init(accempty, 4);
+        *abort_flag = 0;
+        mbar_fence_init();
+        prefetch_tmap(&tm_x);
+        prefetch_tmap(&tm_w);
+        if (SWIGLU) prefetch_tmap(&tm_w2);
+        if (p.ktl) prefetch_tmap(&tm_t);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+                const int wt = tile % p.num_w_tiles, tt = tile / p.num_w_tiles;
+                for (int kt = 0; kt < KT; ++kt, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY))
+                        break;
+                    uint8_t *xs = smem + C::SMEM_X + s * X_STAGE_BYTES;
+                    uint8_t *ws = smem + C::SMEM_W + s * C::W_STAGE_BYTES;
+                    if (kt < p.ktw) {
+                        mbar_arrive_expect_tx(&full[s], X_STAGE_BYTES + C::W_STAGE_BYTES);
+                        tma_load_2d(xs, &tm_x, &full[s], kt * BK, tt * BT);
+                        if (SWIGLU) {
+                            tma_load_2d(ws, &tm_w, &full[s], kt * C::W_BOX_WORDS, wt * 64);
+                            tma_load_2d(ws + 64 * C::W_ROW_BYTES, &tm_w2, &full[s], kt * C::W_BOX_WORDS,
+                                        wt * 64);
+                        } else {
+                            tma_load_2d(ws, &tm_w, &full[s], kt * C::W_BOX_WORDS, wt * BW);
+                        }
+                    } else {
+                        mbar_arrive_expect_tx(&full[s], X_STAGE_BYTES);
+                        tma_load_2d(xs, &tm_t, &full[s], (kt - p.ktw) * BK, tt * BT);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16(BW, BT);
+            uint32_t it = 0, tcount = 0;
+            for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++tcount) {
+                if (!mbar_wait(accempty, (tcount & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_ACC)) break;
+                tc_fence_after();
+                bool ok = true;
+                for (int kt = 0; kt < KT; ++kt, ++it) {
+                    const int s = it % STAGES, j = it % AST;
+                    if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL) ||
+                        !mbar_wait(&afull[j], (it / AST) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t bdesc =
+                        umma_desc_k_sw128(smem_u32(smem + C::SMEM_X + s * X_STAGE_BYTES));
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        tc_mma_ts(tmem + ACC_COL, tmem + A_COL + j * 32 + kk * 8, bdesc + 2 * kk, idesc,
+                                  (kt | kk) != 0);
+                    tc_commit(&empty[s]);
+                    tc_commit(&aempty[j]);
+                }
+                if (!ok) break;
+                tc_commit(accfull);
+            }
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ---------------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        const int row = q * 32 + lane;  // TMEM lane == weight row within the tile
+        float *xch = reinterpret_cast<float *>(smem + C::SMEM_XCH);
+        uint32_t tcount = 0;
+        for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++tcount) {
+            const int wt = tile % p.num_w_tiles, tt = tile / p.num_w_tiles;
+            if (!mbar_wait(accfull, tcount & 1, abort_flag, DEV_ERR_TIMEOUT_ACC)) break;
+            tc_fence_after();
+            int n;
+            float bias = 0.f;
+            bool has_bias;
+            if (SWIGLU) {
+                n = wt * 64 + (row & 63);
+                const __nv_bfloat16 *bp = row < 64 ? p.bias : p.bias2;
+                has_bias = bp != nullptr;
+                if (has_bias && n < p.N) bias = __bfloat162float(bp[n]);
+            } else {
+                n = wt * BW + row;
+                has_bias = p.bias != nullptr;
+                if (has_bias && n < p.N) bias = __bfloat162float(p.bias[n]);
+            }
+            const int m0 = tt * BT;
+#pragma unroll 1
+            for (int c = 0; c < BT / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ACC_COL + ((uint32_t)(q * 32) << 16) + c * 32, v);
+                tmem_ld_wait();
+                if (c == BT / 32 - 1) {
+                    // accumulator fully read: let the MMA warp start the next tile
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(accempty);
+                }
+                if (SWIGLU) {
+                    if (row >= 64) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            xch[(row - 64) * 33 + i] =
+                                epi_value(__uint_as_float(v[i]), bias, has_bias, QL_ACT_NONE);
+                    }
+                    named_bar_sync(1, 128);
+                    if (row < 64 && n < p.N) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const int m = m0 + c * 32 + i;
+                            const float g = epi_value(__uint_as_float(v[i]), bias, has_bias, QL_ACT_NONE);
+                            const float u = xch[row * 33 + i];
+                            if (m < p.M) p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(silu_f(g) * u);
+                        }
+                    }
+                    named_bar_sync(1, 128);
+                } else if (n < p.N) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int m = m0 + c * 32 + i;
+                        if (m < p.M)
+                            p.y[(int64_t)m * p.N + n] =
+                                __float2bfloat16_rn(epi_value(__uint_as_float(v[i]), bias, has_bias, p.act));
+                    }
+                }
+            }
+        }
+    } else if (warp >= 8) {
+        // ---------------------------------------------------------------- dequant warpgroups
+        const int wg = (warp - 8) >> 2, q = warp & 3;
+        const int row = q * 32 + lane;
+        const uint32_t taddr_lane = tmem + ((uint32_t)(q * 32) << 16) + A_COL;
+        uint32_t it = 0;
+        for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+            const int wt = tile % p.num_w_tiles;
+            int n;
+            const __nv_bfloat16 *sc, *bi;
+            if (SWIGLU) {
+                n = wt * 64 + (row & 63);
+                sc = row < 64 ? p.scales : p.scales2;
+                bi = row < 64 ? p.biases : p.biases2;
+            } else {
+                n = wt * BW + row;
+                sc = p.scales;
+                bi = p.biases;
+            }
+            const bool row_ok = n < p.N;
+            bool ok = true;
+            for (int kt = 0; kt < KT; ++kt, ++it) {
+                if ((int)(it & 1) != wg) continue;
+                const int s = it % STAGES, j = it % AST;
+                if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL) ||
+                    !mbar_wait(&aempty[j], ((it / AST) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY)) {
+                    ok = false;
+                    break;
+                }
+                uint32_t r[32];
+                if (kt < p.ktw) {
+                    const int k0 = kt * BK;
+                    const int g0 = k0 / p.gs, g1 = (k0 + 32) / p.gs;
+                    uint32_t s0 = 0, b0 = 0, s1 = 0, b1 = 0;  // bf16x2 broadcast pairs
+                    if (row_ok) {
+                        const uint16_t *sp = reinterpret_cast<const uint16_t *>(sc) + (int64_t)n * p.G;
+                        const uint16_t *bp = reinterpret_cast<const uint16_t *>(bi) + (int64_t)n * p.G;
+                        if (g0 < p.G) {
+                            s0 = sp[g0] * 0x10001u;
+                            b0 = bp[g0] * 0x10001u;
+                        }
+                        if (g1 < p.G) {
+                            s1 = sp[g1] * 0x10001u;
+                            b1 = bp[g1] * 0x10001u;
+                        }
+                    }
+                    const uint8_t *wrow = smem + C::SMEM_W + s * C::W_STAGE_BYTES + row * C::W_ROW_BYTES;
+                    if constexpr (BITS == 4) {
+                        uint4 a = reinterpret_cast<const uint4 *>(wrow)[0];
+                        uint4 b = reinterpret_cast<const uint4 *>(wrow)[1];
+                        const uint32_t wv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            uint32_t qp[4];
+                            q4_word_to_bf16_pairs(wv[i], qp);
+                            const uint32_t ss = i < 4 ? s0 : s1, bb = i < 4 ? b0 : b1;
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) r[4 * i + t] = hfma2_bf16(qp[t], ss, bb);
+                        }
+                    } else {
+                        const float fs0 = bf16lo(s0), fb0 = bf16lo(b0), fs1 = bf16lo(s1), fb1 = bf16lo(b1);
+#pragma unroll
+                        for (int h = 0; h < 4; ++h) {
+                            uint4 a = reinterpret_cast<const uint4 *>(wrow)[h];
+                            const uint32_t wv[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const int wi = 4 * h + i;  // word index: codes 4wi..4wi+3
+                                const float ss = wi < 8 ? fs0 : fs1, bb = wi < 8 ? fb0 : fb1;
+                                const float c0 = fmaf(q8_code_f32(wv[i], 0), ss, bb);
+                                const float c1 = fmaf(q8_code_f32(wv[i], 1), ss, bb);
+                                const float c2 = fmaf(q8_code_f32(wv[i], 2), ss, bb);
+                                const float c3 = fmaf(q8_code_f32(wv[i], 3), ss, bb);
+                                r[2 * wi] = pack_bf16x2(c0, c1);
+                                r[2 * wi + 1] = pack_bf16x2(c2, c3);
+                            }
+                        }
+                    }
+                } else {
+                    // LoRA step: A = B^T rows for this tile, columns [64l, 64l + 64) of rank.
+                    const int l0 = (kt - p.ktw) * BK;
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) {
+                        const int j0 = l0 + 2 * c;
+                        uint32_t lo = 0, hi = 0;
+                        if (row_ok && j0 < p.lora_rank)
+                            lo = reinterpret_cast<const uint16_t *>(p.lora_b)[(int64_t)j0 * p.N + n];
+                        if (row_ok && j0 + 1 < p.lora_rank)
+                            hi = reinterpret_cast<const uint16_t *>(p.lora_b)[(int64_t)(j0 + 1) * p.N + n];
+                        r[c] = lo | (hi << 16);
+                    }
+                }
+                tmem_st32(taddr_lane + j * 32, r);
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&afull[j]);
+                    mbar_arrive(&empty[s]);
+                }
+            }
+            if (!ok) break;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                    const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                    const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode() {
+    static PFN_encodeTiled fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_encodeTiled>(ptr);
+    }
+    return fn;
+}
+
+static int make_map_2d(CUtensorMap *map, CUtensorMapDataType dt, int elem_bytes, const void *base,
+                       uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                       uint32_t box_outer, CUtensorMapSwizzle sw) {
+    PFN_encodeTiled enc = get_encode();
+    if (!enc) return fail(QL_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_stride_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    (void)elem_bytes;
+    CUresult r = enc(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(QL_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return QL_OK;
+}
+
+template <int BITS, bool SWIGLU>
+static int launch_t(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mw2,
+                    const CUtensorMap &mt, const Params &p, cudaStream_t st) {
+    using C = Cfg<BITS>;
+    auto kfn = qgemm_kernel<BITS, SWIGLU>;
+    static bool configured = false;  // per template instance; attribute is per-function
+    if (!configured) {
+        QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_TOTAL));
+        configured = true;
+    }
+    int dev = 0, sms = 148;
+    QL_CUDA_TRY(cudaGetDevice(&dev));
+    QL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int tiles = p.num_w_tiles * p.num_t_tiles;
+    const int grid = tiles < sms ? tiles : sms;
+    kfn<<<grid, NTHREADS, C::SMEM_TOTAL, st>>>(mx, mw, mw2, mt, p);
+    QL_CUDA_TRY(cudaGetLastError());
+    return QL_OK;
+}
+
+}  // namespace gemm
+
+// x [M,K] bf16, W packed [N,K] (+ W3 for SwiGLU), scales/biases bf16.
+// lora_t: [M, r_pad] bf16 (r_pad = round_up(rank, 64)) already holding s.(x.A), or null.
+int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales,
+                       const void *biases, const uint32_t *wq2, const void *scales2,
+                       const void *biases2, int64_t N, int gs, int bits, const void *bias,
+                       const void *bias2, int act, const void *lora_t, const void *lora_b,
+                       int64_t rank, void *y, cudaStream_t st) {
+    using namespace gemm;
+    const bool swiglu = act == QL_ACT_SWIGLU;
+    Params p{};
+    p.M = (int)M;
+    p.N = (int)N;
+    p.K = (int)K;
+    p.gs = gs;
+    p.G = (int)(K / gs);
+    p.ktw = (int)((K + BK - 1) / BK);
+    const int64_t rpad = rank > 0 ? (rank + BK - 1) / BK * BK : 0;
+    p.ktl = (int)(rpad / BK);
+    p.act = act;
+    p.num_w_tiles = (int)((N + (swiglu ? 64 : BW) - 1) / (swiglu ? 64 : BW));
+    p.num_t_tiles = (int)((M + BT - 1) / BT);
+    p.scales = (const __nv_bfloat16 *)scales;
+    p.biases = (const __nv_bfloat16 *)biases;
+    p.scales2 = (const __nv_bfloat16 *)scales2;
+    p.biases2 = (const __nv_bfloat16 *)biases2;
+    p.bias = (const __nv_bfloat16 *)bias;
+    p.bias2 = (const __nv_bfloat16 *)bias2;
+    p.lora_b = (const __nv_bfloat16 *)lora_b;
+    p.lora_rank = (int)rank;
+    p.y = (__nv_bfloat16 *)y;
+
+    CUtensorMap mx, mw, mw2, mt;
+    int rc = make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, (uint64_t)K, (uint64_t)M,
+                         (uint64_t)K * 2, BK, BT, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    const uint64_t words = (uint64_t)K * bits / 32;
+    const uint32_t box_words = (uint32_t)(BK * bits / 32);
+    const uint32_t box_rows = swiglu ? 64 : BW;
+    rc = make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wq, words, (uint64_t)N, words * 4, box_words,
+                     box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    mw2 = mw;
+    if (swiglu) {
+        rc = make_map_2d(&mw2, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wq2, words, (uint64_t)N, words * 4,
+                         box_words, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+    }
+    mt = mx;
+    if (rpad) {
+        rc = make_map_2d(&mt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, lora_t, (uint64_t)rpad, (uint64_t)M,
+                         (uint64_t)rpad * 2, BK, BT, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    if (bits == 4)
+        return swiglu ? launch_t<4, true>(mx, mw, mw2, mt, p, st) : launch_t<4, false>(mx, mw, mw2, mt, p, st);
+    return swiglu ? launch_t<8, true>(mx, mw, mw2, mt, p, st) : launch_t<8, false>(mx, mw, mw2, mt, p, st);
+}
+
+}  // namespace ql

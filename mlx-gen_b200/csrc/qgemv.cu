@@ -1,0 +1,250 @@
+// qgemv.cu -- small-M (M <= 8) quantized matmul for LLM decode.
+//
+// y[M, N] = x[M, K] . dequant(W)[N, K]^T, bf16 activations and scales, fp32
+// accumulation.  This is the M <= 8 arm of quantized_matmul (the reference's
+// decode-time and adaLN/timestep callers, e.g. mlx-gen-z-image/src/transformer_block.rs:122).
+//
+// The kernel is HBM-bound: every packed byte of W is read once, with 16-byte
+// coalesced loads (four lanes cover 64 contiguous bytes of a row).  The
+// dequantized weights go straight from registers into legacy warp-level MMAs
+// (m16n8k16, bf16 -> fp32): with at most 8 tokens the tensor-core work is tiny
+// and register-resident operands avoid any shared-memory staging; the
+// roofline that matters is HBM bandwidth, not MMA throughput.
+//
+// Decomposition: a CTA of 8 warps owns one strip of 16 weight rows; its warps
+// split K in chunks of 128 (each lane covers 32 consecutive codes of two rows,
+// g and g+8).  Partial 16x8 tiles are summed through shared memory and the
+// fused epilogue (bias, LoRA, GELU / SwiGLU) writes y.
+//
+// Dequantized weights are exact bf16 roundings of fma(code, scale, bias) --
+// the same values ql_dequantize produces -- so GEMV, GEMM and dequant+matmul
+// agree on the operand.
+#include "ql_common.cuh"
+
+namespace ql {
+namespace gemv {
+
+constexpr int WARPS = 8;
+constexpr int CHUNK = 128;  // K per warp step (4 lanes x 32 codes)
+
+struct Params {
+    const __nv_bfloat16 *x;  // [M, K]
+    int M, N, K, gs, G;
+    const uint32_t *wq, *wq2;
+    const uint16_t *scales, *biases, *scales2, *biases2;
+    const __nv_bfloat16 *bias, *bias2;
+    const __nv_bfloat16 *lora_t;  // [M, rpad] = s.(x.A), or null
+    const __nv_bfloat16 *lora_b;  // [rank, N]
+    int rank, rpad;
+    int act;
+    __nv_bfloat16 *y;
+};
+
+__device__ __forceinline__ void mma16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 ldg16(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// Accumulate one chunk (this lane's 32 codes of rows g and g+8) into d.
+template <int BITS>
+__device__ __forceinline__ void chunk_mma(float d[4], const uint32_t *wg_words, const uint32_t *wh_words,
+                                          uint32_t sg, uint32_t bg, uint32_t sh, uint32_t bh,
+                                          const uint4 xv[4]) {
+    if constexpr (BITS == 4) {
+        // 4 words per row; word i holds codes 8i..8i+7.  Pairs (j, j+4) come out of
+        // a word with one shift+mask; x is permuted the same way.
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            uint32_t pg[4], ph[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                pg[j] = hfma2_bf16(hsub2_bf16(((wg_words[i] >> (4 * j)) & 0x000f000fu) | 0x43004300u, 0x43004300u),
+                                   sg, bg);
+                ph[j] = hfma2_bf16(hsub2_bf16(((wh_words[i] >> (4 * j)) & 0x000f000fu) | 0x43004300u, 0x43004300u),
+                                   sh, bh);
+            }
+            const uint4 X = xv[i];  // x codes 8i..8i+7 as (0,1) (2,3) (4,5) (6,7)
+            const uint32_t x04 = prmt(X.x, X.z, 0x5410u), x15 = prmt(X.x, X.z, 0x7632u);
+            const uint32_t x26 = prmt(X.y, X.w, 0x5410u), x37 = prmt(X.y, X.w, 0x7632u);
+            const uint32_t a0[4] = {pg[0], ph[0], pg[1], ph[1]};
+            mma16816(d, a0, x04, x15);
+            const uint32_t a1[4] = {pg[2], ph[2], pg[3], ph[3]};
+            mma16816(d, a1, x26, x37);
+        }
+    } else {
+        // 8 words per row; word i holds codes 4i..4i+3 (natural pairs).
+        const float fsg = bf16lo(sg), fbg = bf16lo(bg), fsh = bf16lo(sh), fbh = bf16lo(bh);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // two words (8 codes) per step
+            uint32_t pg[4], ph[4];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t wg = wg_words[2 * i + h], wh = wh_words[2 * i + h];
+                pg[2 * h] = pack_bf16x2(fmaf(q8_code_f32(wg, 0), fsg, fbg), fmaf(q8_code_f32(wg, 1), fsg, fbg));
+                pg[2 * h + 1] = pack_bf16x2(fmaf(q8_code_f32(wg, 2), fsg, fbg), fmaf(q8_code_f32(wg, 3), fsg, fbg));
+                ph[2 * h] = pack_bf16x2(fmaf(q8_code_f32(wh, 0), fsh, fbh), fmaf(q8_code_f32(wh, 1), fsh, fbh));
+                ph[2 * h + 1] = pack_bf16x2(fmaf(q8_code_f32(wh, 2), fsh, fbh), fmaf(q8_code_f32(wh, 3), fsh, fbh));
+            }
+            const uint4 X = xv[i];  // x codes 8i..8i+7
+            const uint32_t a0[4] = {pg[0], ph[0], pg[1], ph[1]};
+            mma16816(d, a0, X.x, X.y);
+            const uint32_t a1[4] = {pg[2], ph[2], pg[3], ph[3]};
+            mma16816(d, a1, X.z, X.w);
+        }
+    }
+}
+
+template <int BITS, bool SWIGLU>
+__global__ void __launch_bounds__(WARPS * 32) qgemv_kernel(const Params p) {
+    constexpr int LANE_BYTES = 32 * BITS / 8;  // packed bytes per lane per row per chunk
+    constexpr int NW = LANE_BYTES / 4;         // words
+    __shared__ float red[SWIGLU ? 2 : 1][WARPS][16][8];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, c = lane & 3;
+    const int n0 = blockIdx.x * 16;
+    const int rg = min(n0 + g, p.N - 1), rh = min(n0 + g + 8, p.N - 1);  // clamped rows (stores masked)
+    const int64_t wpr = (int64_t)p.K * BITS / 32;  // words per row
+    const int nchunks = (p.K + CHUNK - 1) / CHUNK;
+
+    float d[4] = {0.f, 0.f, 0.f, 0.f}, d2[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int ch = warp; ch < nchunks; ch += WARPS) {
+        // K % 32 == 0, so a lane's 32-code block is all-in or all-out.  Lanes past
+        // K feed zeros (the MMA needs the whole warp converged).
+        const bool kval = ch * CHUNK + 32 * c < p.K;
+        const int k = kval ? ch * CHUNK + 32 * c : 0;
+        const int grp = k / p.gs;
+        // x for token g (zero for padded tokens)
+        uint4 xv[4];
+        if (g < p.M && kval) {
+            const uint4 *xp = reinterpret_cast<const uint4 *>(p.x + (int64_t)g * p.K + k);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xv[i] = __ldg(xp + i);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xv[i] = make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int pass = 0; pass < (SWIGLU ? 2 : 1); ++pass) {
+            const uint32_t *W = pass ? p.wq2 : p.wq;
+            const uint16_t *S = pass ? p.scales2 : p.scales;
+            const uint16_t *B = pass ? p.biases2 : p.biases;
+            uint32_t wg_words[NW], wh_words[NW];
+            const uint32_t *pgp = W + rg * wpr + (int64_t)k * BITS / 32;
+            const uint32_t *php = W + rh * wpr + (int64_t)k * BITS / 32;
+#pragma unroll
+            for (int v = 0; v < NW / 4; ++v) {
+                uint4 a = make_uint4(0, 0, 0, 0), b = a;
+                if (kval) {
+                    a = ldg16(pgp + 4 * v);
+                    b = ldg16(php + 4 * v);
+                }
+                wg_words[4 * v] = a.x; wg_words[4 * v + 1] = a.y; wg_words[4 * v + 2] = a.z; wg_words[4 * v + 3] = a.w;
+                wh_words[4 * v] = b.x; wh_words[4 * v + 1] = b.y; wh_words[4 * v + 2] = b.z; wh_words[4 * v + 3] = b.w;
+            }
+            const uint32_t sg = __ldg(S + (int64_t)rg * p.G + grp) * 0x10001u;
+            const uint32_t bg = __ldg(B + (int64_t)rg * p.G + grp) * 0x10001u;
+            const uint32_t sh = __ldg(S + (int64_t)rh * p.G + grp) * 0x10001u;
+            const uint32_t bh = __ldg(B + (int64_t)rh * p.G + grp) * 0x10001u;
+            chunk_mma<BITS>(pass ? d2 : d, wg_words, wh_words, sg, bg, sh, bh, xv);
+        }
+    }
+    // D fragment: d[0],d[1] = (row g, tokens 2c, 2c+1); d[2],d[3] = (row g+8, tokens 2c, 2c+1)
+    red[0][warp][g][2 * c] = d[0];
+    red[0][warp][g][2 * c + 1] = d[1];
+    red[0][warp][g + 8][2 * c] = d[2];
+    red[0][warp][g + 8][2 * c + 1] = d[3];
+    if (SWIGLU) {
+        red[SWIGLU ? 1 : 0][warp][g][2 * c] = d2[0];
+        red[SWIGLU ? 1 : 0][warp][g][2 * c + 1] = d2[1];
+        red[SWIGLU ? 1 : 0][warp][g + 8][2 * c] = d2[2];
+        red[SWIGLU ? 1 : 0][warp][g + 8][2 * c + 1] = d2[3];
+    }
+    __syncthreads();
+    if (threadIdx.x < 128) {
+        const int r = threadIdx.x >> 3, m = threadIdx.x & 7;
+        const int n = n0 + r;
+        if (n < p.N && m < p.M) {
+            float acc = 0.f, acc2 = 0.f;
+#pragma unroll
+            for (int w = 0; w < WARPS; ++w) {
+                acc += red[0][w][r][m];
+                if (SWIGLU) acc2 += red[SWIGLU ? 1 : 0][w][r][m];
+            }
+            if (p.lora_t) {
+                const __nv_bfloat16 *t = p.lora_t + (int64_t)m * p.rpad;
+                for (int j = 0; j < p.rank; ++j)
+                    acc += __bfloat162float(t[j]) * __bfloat162float(p.lora_b[(int64_t)j * p.N + n]);
+            }
+            float v = round_bf16(acc);
+            if (p.bias) v = round_bf16(v + __bfloat162float(p.bias[n]));
+            if (SWIGLU) {
+                float u = round_bf16(acc2);
+                if (p.bias2) u = round_bf16(u + __bfloat162float(p.bias2[n]));
+                v = v / (1.0f + __expf(-v)) * u;
+            } else if (p.act == QL_ACT_GELU_TANH) {
+                float t;
+                const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+                asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(inner));
+                v = 0.5f * v * (1.0f + t);
+            } else if (p.act == QL_ACT_GELU_ERF) {
+                v = 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
+            }
+            p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(v);
+        }
+    }
+}
+
+}  // namespace gemv
+
+int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales,
+                 const void *biases, const uint32_t *wq2, const void *scales2, const void *biases2,
+                 int64_t N, int gs, int bits, const void *bias, const void *bias2, int act,
+                 const void *lora_t, const void *lora_b, int64_t rank, void *y, cudaStream_t st) {
+    using namespace gemv;
+    Params p{};
+    p.x = (const __nv_bfloat16 *)x;
+    p.M = (int)M;
+    p.N = (int)N;
+    p.K = (int)K;
+    p.gs = gs;
+    p.G = (int)(K / gs);
+    p.wq = wq;
+    p.wq2 = wq2;
+    p.scales = (const uint16_t *)scales;
+    p.biases = (const uint16_t *)biases;
+    p.scales2 = (const uint16_t *)scales2;
+    p.biases2 = (const uint16_t *)biases2;
+    p.bias = (const __nv_bfloat16 *)bias;
+    p.bias2 = (const __nv_bfloat16 *)bias2;
+    p.lora_t = (const __nv_bfloat16 *)lora_t;
+    p.lora_b = (const __nv_bfloat16 *)lora_b;
+    p.rank = (int)rank;
+    p.rpad = (int)(rank > 0 ? (rank + 63) / 64 * 64 : 0);
+    p.act = act;
+    p.y = (__nv_bfloat16 *)y;
+    const int grid = (int)((N + 15) / 16);
+    const bool sw = act == QL_ACT_SWIGLU;
+    if (bits == 4) {
+        if (sw) qgemv_kernel<4, true><<<grid, WARPS * 32, 0, st>>>(p);
+        else qgemv_kernel<4, false><<<grid, WARPS * 32, 0, st>>>(p);
+    } else {
+        if (sw) qgemv_kernel<8, true><<<grid, WARPS * 32, 0, st>>>(p);
+        else qgemv_kernel<8, false><<<grid, WARPS * 32, 0, st>>>(p);
+    }
+    QL_CUDA_TRY(cudaGetLastError());
+    return QL_OK;
+}
+
+}  // namespace ql

@@ -1,0 +1,163 @@
+"""numpy/ctypes front end of the CPU oracle (oracle/qref.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, ``__graft_entry__.smoke()`` and the
+CPU-baseline legs of ``bench.py``.  The product library never imports it.
+
+bf16 arrays are carried as ``np.uint16`` bit patterns; f32 as ``np.float32``;
+f16 as ``np.float16``.  Every function mirrors one entry point of qref.c, which
+cites the reference file:line it restates.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+F32, BF16, F16 = 0, 1, 2
+ACT_NONE, ACT_GELU_TANH, ACT_GELU_ERF = 0, 1, 2
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_ref", "libqref.so")
+_lib = None
+
+
+def build() -> str:
+    """Compile qref.c with oracle/Makefile (a no-op when up to date)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = C.CDLL(_LIB_PATH)
+        i64, vp, i32 = C.c_int64, C.c_void_p, C.c_int
+        L.qref_quantize.argtypes = [vp, i32, i64, i64, i32, i32, vp, vp, vp, i32]
+        L.qref_dequantize.argtypes = [vp, vp, vp, i32, i64, i64, i32, i32, vp, i64, vp, i32]
+        L.qref_qmm.argtypes = [vp, i32, i64, i64, vp, vp, vp, i32, i64, i32, i32, vp, i32,
+                               vp, vp, i64, C.c_float, vp, i32]
+        L.qref_qmm_fast.argtypes = [vp, i32, i64, i64, vp, vp, vp, i32, i64, i32, i32, vp, vp,
+                                    i32, i32]
+        L.qref_swiglu.argtypes = [vp, vp, i64, i32, vp]
+        L.qref_f32_to_bf16.argtypes = [vp, vp, i64]
+        for f in (L.qref_quantize, L.qref_dequantize, L.qref_qmm, L.qref_qmm_fast):
+            f.restype = i32
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def dtype_code(a: np.ndarray) -> int:
+    if a.dtype == np.float32:
+        return F32
+    if a.dtype == np.uint16:
+        return BF16
+    if a.dtype == np.float16:
+        return F16
+    raise TypeError(f"unsupported dtype {a.dtype}")
+
+
+def np_dtype(code: int):
+    return {F32: np.float32, BF16: np.uint16, F16: np.float16}[code]
+
+
+def to_bf16(a: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 bits, round to nearest even."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    out = np.empty(a.shape, np.uint16)
+    lib().qref_f32_to_bf16(_p(a), _p(out), a.size)
+    return out
+
+
+def bf16_to_f32(a: np.ndarray) -> np.ndarray:
+    return (a.astype(np.uint32) << 16).view(np.float32)
+
+
+def to_f32(a: np.ndarray) -> np.ndarray:
+    return bf16_to_f32(a) if a.dtype == np.uint16 else a.astype(np.float32)
+
+
+def quantize(w: np.ndarray, group_size: int = 64, bits: int = 4, sb_dtype: int | None = None):
+    """(wq u32 [N, K*bits/32], scales [N, K/gs], biases [N, K/gs]); scales in w's dtype."""
+    w = np.ascontiguousarray(w)
+    N, K = w.shape
+    sd = dtype_code(w) if sb_dtype is None else sb_dtype
+    wq = np.empty((N, K * bits // 32), np.uint32)
+    s = np.empty((N, K // group_size), np_dtype(sd))
+    b = np.empty_like(s)
+    rc = lib().qref_quantize(_p(w), dtype_code(w), N, K, group_size, bits, _p(wq), _p(s), _p(b), sd)
+    if rc:
+        raise ValueError(f"qref_quantize rc={rc}")
+    return wq, s, b
+
+
+def dequantize(wq, scales, biases, group_size=64, bits=4, ids=None, out_dtype=None):
+    wq = np.ascontiguousarray(wq, np.uint32)
+    N, G = scales.shape
+    K = G * group_size
+    od = dtype_code(scales) if out_dtype is None else out_dtype
+    rows = N
+    idp = None
+    if ids is not None:
+        ids = np.ascontiguousarray(ids, np.int64).reshape(-1)
+        rows = ids.size
+        idp = ids
+    out = np.empty((rows, K), np_dtype(od))
+    rc = lib().qref_dequantize(_p(wq), _p(np.ascontiguousarray(scales)), _p(np.ascontiguousarray(biases)),
+                               dtype_code(scales), N, K, group_size, bits, _p(idp), rows, _p(out), od)
+    if rc:
+        raise ValueError(f"qref_dequantize rc={rc}")
+    return out
+
+
+def quantized_matmul(x, wq, scales, biases, group_size=64, bits=4, bias=None, act=ACT_NONE,
+                     lora_a=None, lora_b=None, lora_scale=1.0, out_dtype=None):
+    """Exact-mode y = x . dequant(W)^T with the reference's rounding points (see qref.c)."""
+    x = np.ascontiguousarray(x)
+    M, K = x.shape
+    N = scales.shape[0]
+    od = dtype_code(x) if out_dtype is None else out_dtype
+    y = np.empty((M, N), np_dtype(od))
+    rank = 0 if lora_a is None else lora_a.shape[1]
+    rc = lib().qref_qmm(_p(x), dtype_code(x), M, K, _p(np.ascontiguousarray(wq, np.uint32)),
+                        _p(np.ascontiguousarray(scales)), _p(np.ascontiguousarray(biases)),
+                        dtype_code(scales), N, group_size, bits,
+                        _p(None if bias is None else np.ascontiguousarray(bias)), act,
+                        _p(None if lora_a is None else np.ascontiguousarray(lora_a)),
+                        _p(None if lora_b is None else np.ascontiguousarray(lora_b)),
+                        rank, float(lora_scale), _p(y), od)
+    if rc:
+        raise ValueError(f"qref_qmm rc={rc}")
+    return y
+
+
+def quantized_matmul_fast(x, wq, scales, biases, group_size=64, bits=4, bias=None, threads=None):
+    """The timed CPU baseline (fp32 accumulation, pthreads)."""
+    x = np.ascontiguousarray(x)
+    M, K = x.shape
+    N = scales.shape[0]
+    od = dtype_code(x)
+    y = np.empty((M, N), np_dtype(od))
+    nt = threads or os.cpu_count() or 1
+    rc = lib().qref_qmm_fast(_p(x), od, M, K, _p(np.ascontiguousarray(wq, np.uint32)),
+                             _p(np.ascontiguousarray(scales)), _p(np.ascontiguousarray(biases)),
+                             dtype_code(scales), N, group_size, bits,
+                             _p(None if bias is None else np.ascontiguousarray(bias)), _p(y), od, nt)
+    if rc:
+        raise ValueError(f"qref_qmm_fast rc={rc}")
+    return y
+
+
+def swiglu(a, b):
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    out = np.empty_like(a)
+    lib().qref_swiglu(_p(a), _p(b), a.size, dtype_code(a), _p(out))
+    return out

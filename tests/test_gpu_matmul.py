@@ -1,0 +1,135 @@
+"""GPU parity: quantized_matmul (GEMV, tcgen05 GEMM, generic) and its fused epilogues
+against the oracle, within the stated bf16 tolerance (tests/helpers.py
+assert_bf16_close: 2 bf16 ulps + 2e-3 of the output scale element-wise, relative L2
+<= 4e-3; activation epilogues, which the reference rounds op by op in bf16, get 4 ulps)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+import qlinear
+from helpers import assert_bf16_close, np2t, rand_bf16, t2np
+
+pytestmark = pytest.mark.gpu
+GEMV, GEMM, GENERIC = qlinear.KERNEL_GEMV, qlinear.KERNEL_GEMM, qlinear.KERNEL_GENERIC
+
+
+def make_case(dev, M, N, K, gs, bits, seed, wstd=0.02):
+    rng = np.random.default_rng(seed)
+    w = rand_bf16((N, K), wstd, rng)
+    x = rand_bf16((M, K), 1.0, rng)
+    wq, s, b = O.quantize(w, gs, bits)
+    return rng, x, wq, s, b, np2t(x, dev), np2t(wq, dev), np2t(s, dev), np2t(b, dev)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_fixture_qmm_f32(golden, dev, bits):
+    """f32 activations and scales (generic kernel) vs the MLX golden qmm
+    (reference gate allclose 1e-2/1e-2, tests/quant_parity.rs:59-64)."""
+    p = f"q{bits}_"
+    y = qlinear.quantized_matmul(np2t(golden["x"], dev), np2t(golden[p + "wq"], dev),
+                                 np2t(golden[p + "scales"], dev), np2t(golden[p + "biases"], dev), True, 64, bits)
+    np.testing.assert_allclose(t2np(y), golden[p + "qmm"], rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("gs", [32, 64, 128])
+@pytest.mark.parametrize("M", [1, 2, 3, 8])
+def test_gemv_parity(dev, bits, gs, M):
+    N, K = 200, 384
+    _, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 100 * M + gs + bits)
+    y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, kernel=GEMV)
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(O.quantized_matmul(x, wq, s, b, gs, bits)), what="gemv")
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("gs", [32, 64, 128])
+@pytest.mark.parametrize("M,N,K", [(9, 128, 64), (256, 128, 256), (300, 200, 448), (513, 384, 128)])
+def test_gemm_parity(dev, bits, gs, M, N, K):
+    if K % gs:
+        pytest.skip("K must be a multiple of the group size")
+    _, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, M + N + K + gs + bits)
+    y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, kernel=GEMM)
+    torch.cuda.synchronize()
+    assert qlinear.device_error() == 0
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(O.quantized_matmul(x, wq, s, b, gs, bits)), what="gemm")
+
+
+@pytest.mark.parametrize("kernel", [GEMV, GEMM, GENERIC])
+@pytest.mark.parametrize("act", [None, "gelu_tanh", "gelu"])
+def test_bias_act_epilogue(dev, kernel, act):
+    M = 4 if kernel == GEMV else 260
+    N, K, gs, bits = 192, 256, 64, 8
+    rng, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 5)
+    bias = rand_bf16((N,), 0.5, rng)
+    y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, bias=np2t(bias, dev), act=act, kernel=kernel)
+    code = {None: O.ACT_NONE, "gelu_tanh": O.ACT_GELU_TANH, "gelu": O.ACT_GELU_ERF}[act]
+    ref = O.quantized_matmul(x, wq, s, b, gs, bits, bias=bias, act=code)
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), ulps=4 if act else 2, what=f"bias+{act}")
+
+
+@pytest.mark.parametrize("kernel", [GEMV, GEMM, GENERIC])
+@pytest.mark.parametrize("bits", [4, 8])
+def test_swiglu_epilogue(dev, kernel, bits):
+    M = 5 if kernel == GEMV else 300
+    N, K, gs = 160, 320, 64
+    rng, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 9)
+    w3 = rand_bf16((N, K), 0.02, rng)
+    wq3, s3, b3 = O.quantize(w3, gs, bits)
+    y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, act="swiglu",
+                                 up=(np2t(wq3, dev), np2t(s3, dev), np2t(b3, dev)), kernel=kernel)
+    h1 = O.quantized_matmul(x, wq, s, b, gs, bits)
+    h3 = O.quantized_matmul(x, wq3, s3, b3, gs, bits)
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(O.swiglu(h1, h3)), ulps=4, what="swiglu")
+
+
+@pytest.mark.parametrize("kernel", [GEMV, GEMM, GENERIC])
+@pytest.mark.parametrize("rank", [8, 32, 96])
+def test_lora_epilogue(dev, kernel, rank):
+    """LoRA residual scale*(x.A).B fused into the accumulator (src/adapters.rs:260-270)."""
+    M = 7 if kernel == GEMV else 270
+    N, K, gs, bits = 256, 384, 64, 4
+    rng, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, rank)
+    A = rand_bf16((K, rank), 1.0 / np.sqrt(rank), rng)
+    B = rand_bf16((rank, N), 0.01, rng)
+    bias = rand_bf16((N,), 0.1, rng)
+    y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, bias=np2t(bias, dev),
+                                 lora=(np2t(A, dev), np2t(B, dev), 0.75), kernel=kernel)
+    ref = O.quantized_matmul(x, wq, s, b, gs, bits, bias=bias, lora_a=A, lora_b=B, lora_scale=0.75)
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), ulps=3, what=f"lora r{rank}")
+
+
+def test_kernels_agree_with_each_other(dev):
+    """GEMM, GEMV (M<=8 slices) and the generic kernel on the same operands."""
+    M, N, K, gs, bits = 8, 512, 1024, 64, 4
+    _, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 3)
+    ys = [t2np(qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, kernel=k)) for k in (GEMV, GEMM, GENERIC)]
+    for y in ys[1:]:
+        assert_bf16_close(O.to_f32(y), O.to_f32(ys[0]), what="cross-kernel")
+
+
+@pytest.mark.parametrize("bits,N,K,act", [(8, 12288, 3072, "gelu_tanh"), (4, 3072, 3072, None),
+                                          (4, 5120, 13824, None)])
+def test_full_size_gemm_properties(dev, bits, N, K, act):
+    """BASELINE shapes at full size (FLUX MLP-up Q8, cfg1 Q4, Wan FFN-down Q4), M=4608:
+    (1) rows sampled across the whole output match the oracle; (2) the GEMM equals
+    dequantize -> fp32 matmul (a size-independent identity)."""
+    M, gs = 4608, 64
+    g = torch.Generator(device=dev).manual_seed(1)
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    bias = (torch.randn(N, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    wq, s, b = qlinear.quantize(w, gs, bits)
+    y = qlinear.quantized_matmul(x, wq, s, b, True, gs, bits, bias=bias, act=act, kernel=GEMM)
+    torch.cuda.synchronize()
+    assert qlinear.device_error() == 0
+    rows = [0, 1, 255, 256, 2047, 4095, 4352, 4607]
+    code = O.ACT_GELU_TANH if act else O.ACT_NONE
+    ref = O.quantized_matmul(t2np(x[rows]), t2np(wq), t2np(s), t2np(b), gs, bits, bias=t2np(bias), act=code)
+    assert_bf16_close(O.to_f32(t2np(y[rows])), O.to_f32(ref), ulps=4 if act else 2, what="sampled rows")
+    if act is None:
+        d = qlinear.dequantize(wq, s, b, gs, bits).float()
+        ref_all = ((x.float() @ d.t()).to(torch.bfloat16).float() + bias.float()).to(torch.bfloat16).float()
+        err = (y.float() - ref_all).abs()
+        assert err.max() <= ref_all.abs().max() * 2 ** -6
+        assert (err.norm() / ref_all.norm()) <= 4e-3
