@@ -300,8 +300,13 @@ def run_ours(args):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    # clocks are sampled from here to the end of the timed region; a ~1 s untimed soak
+    # first brings the GPU to its steady (power-capped) clock so the samples describe load
     clocks = ClockSampler(local) if rank == 0 else None
-    torch.cuda.synchronize()
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < 1.0:
+        step()
+        torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

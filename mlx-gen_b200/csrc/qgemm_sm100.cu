@@ -42,6 +42,7 @@ constexpr int NTHREADS = 512;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t ACC_COL = 0;
 constexpr uint32_t A_COL = 256;
+constexpr uint32_t STG_COL = 384;   // bf16 staging of the finished tile (128 columns)
 constexpr int X_STAGE_BYTES = BT * BK * 2;  // 32 KB
 
 template <int BITS>
@@ -88,16 +89,6 @@ __device__ __forceinline__ float gelu_erf_f(float x) {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
-// Epilogue value for one output: the reference rounds the matmul to the output
-// dtype, then adds the bias as a separate bf16 op (src/adapters.rs:318-320),
-// then applies the activation.
-__device__ __forceinline__ float epi_value(float acc, float bias, bool has_bias, int act) {
-    float v = round_bf16(acc);
-    if (has_bias) v = round_bf16(v + bias);
-    if (act == QL_ACT_GELU_TANH) v = gelu_tanh_f(v);
-    else if (act == QL_ACT_GELU_ERF) v = gelu_erf_f(v);
-    return v;
-}
 
 template <int BITS, bool SWIGLU>
 __global__ void __launch_bounds__(NTHREADS, 1)
@@ -207,52 +198,74 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     } else if (warp >= 4 && warp < 8) {
         // ---------------------------------------------------------------- epilogue
+        // Phase 1 drains the fp32 accumulator as fast as possible: each 32-column
+        // chunk is rounded (+ bias, rounded again: the reference's two roundings) and
+        // packed to bf16 pairs into the free TMEM columns [STG_COL, STG_COL + 128),
+        // then the accumulator is released so the MMA warp can start the next tile.
+        // Phase 2 reads the staged bf16 values back, applies the activation and
+        // writes y with warp-coalesced stores (32 lanes = 32 consecutive columns).
         const int q = warp & 3;
         const int row = q * 32 + lane;  // TMEM lane == weight row within the tile
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
         float *xch = reinterpret_cast<float *>(smem + C::SMEM_XCH);
         uint32_t tcount = 0;
         for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++tcount) {
             const int wt = tile % p.num_w_tiles, tt = tile / p.num_w_tiles;
-            if (!mbar_wait(accfull, tcount & 1, abort_flag, DEV_ERR_TIMEOUT_ACC)) break;
-            tc_fence_after();
             int n;
-            float bias = 0.f;
-            bool has_bias;
+            const __nv_bfloat16 *bp;
             if (SWIGLU) {
                 n = wt * 64 + (row & 63);
-                const __nv_bfloat16 *bp = row < 64 ? p.bias : p.bias2;
-                has_bias = bp != nullptr;
-                if (has_bias && n < p.N) bias = __bfloat162float(bp[n]);
+                bp = row < 64 ? p.bias : p.bias2;
             } else {
                 n = wt * BW + row;
-                has_bias = p.bias != nullptr;
-                if (has_bias && n < p.N) bias = __bfloat162float(p.bias[n]);
+                bp = p.bias;
             }
+            const bool has_bias = bp != nullptr;
+            const float bias = (has_bias && n < p.N) ? __bfloat162float(bp[n]) : 0.f;
+            if (!mbar_wait(accfull, tcount & 1, abort_flag, DEV_ERR_TIMEOUT_ACC)) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < BT / 32; ++c) {
+                uint32_t v[32], pk[16];
+                tmem_ld32(lane_base + ACC_COL + c * 32, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float a = round_bf16(__uint_as_float(v[2 * i]));
+                    float b = round_bf16(__uint_as_float(v[2 * i + 1]));
+                    if (has_bias) {
+                        a += bias;
+                        b += bias;
+                    }
+                    pk[i] = pack_bf16x2(a, b);
+                }
+                tmem_st16(lane_base + STG_COL + c * 16, pk);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(accempty);  // accumulator free for the next tile
+
             const int m0 = tt * BT;
 #pragma unroll 1
             for (int c = 0; c < BT / 32; ++c) {
-                uint32_t v[32];
-                tmem_ld32(tmem + ACC_COL + ((uint32_t)(q * 32) << 16) + c * 32, v);
+                uint32_t pk[16];
+                tmem_ld16(lane_base + STG_COL + c * 16, pk);
                 tmem_ld_wait();
-                if (c == BT / 32 - 1) {
-                    // accumulator fully read: let the MMA warp start the next tile
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(accempty);
-                }
                 if (SWIGLU) {
                     if (row >= 64) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            xch[(row - 64) * 33 + i] =
-                                epi_value(__uint_as_float(v[i]), bias, has_bias, QL_ACT_NONE);
+                        for (int i = 0; i < 16; ++i) {
+                            xch[(row - 64) * 33 + 2 * i] = bf16lo(pk[i]);
+                            xch[(row - 64) * 33 + 2 * i + 1] = bf16hi(pk[i]);
+                        }
                     }
                     named_bar_sync(1, 128);
                     if (row < 64 && n < p.N) {
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             const int m = m0 + c * 32 + i;
-                            const float g = epi_value(__uint_as_float(v[i]), bias, has_bias, QL_ACT_NONE);
+                            const float g = (i & 1) ? bf16hi(pk[i >> 1]) : bf16lo(pk[i >> 1]);
                             const float u = xch[row * 33 + i];
                             if (m < p.M) p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(silu_f(g) * u);
                         }
@@ -262,115 +275,130 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         const int m = m0 + c * 32 + i;
-                        if (m < p.M)
-                            p.y[(int64_t)m * p.N + n] =
-                                __float2bfloat16_rn(epi_value(__uint_as_float(v[i]), bias, has_bias, p.act));
+                        float v = (i & 1) ? bf16hi(pk[i >> 1]) : bf16lo(pk[i >> 1]);
+                        if (p.act == QL_ACT_GELU_TANH) v = gelu_tanh_f(v);
+                        else if (p.act == QL_ACT_GELU_ERF) v = gelu_erf_f(v);
+                        if (m < p.M) p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(v);
                     }
                 }
             }
         }
     } else if (warp >= 8) {
         // ---------------------------------------------------------------- dequant warpgroups
+        // Warpgroup wg handles this CTA's k-steps it = wg, wg + 2, ... (flattened over
+        // tiles).  The scales / biases of step it+2 are loaded before step it is
+        // processed, so their L2 latency stays off the critical path.
         const int wg = (warp - 8) >> 2, q = warp & 3;
         const int row = q * 32 + lane;
         const uint32_t taddr_lane = tmem + ((uint32_t)(q * 32) << 16) + A_COL;
-        uint32_t it = 0;
-        for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        const int my_tiles = (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        const uint32_t total = (uint32_t)my_tiles * (uint32_t)KT;
+
+        // weight row (global) of this thread for tile `tile`, plus its scale/bias arrays
+        auto row_of = [&](int tile, const uint16_t *&sc, const uint16_t *&bi) -> int {
             const int wt = tile % p.num_w_tiles;
-            int n;
-            const __nv_bfloat16 *sc, *bi;
             if (SWIGLU) {
-                n = wt * 64 + (row & 63);
-                sc = row < 64 ? p.scales : p.scales2;
-                bi = row < 64 ? p.biases : p.biases2;
-            } else {
-                n = wt * BW + row;
-                sc = p.scales;
-                bi = p.biases;
+                sc = reinterpret_cast<const uint16_t *>(row < 64 ? p.scales : p.scales2);
+                bi = reinterpret_cast<const uint16_t *>(row < 64 ? p.biases : p.biases2);
+                return wt * 64 + (row & 63);
             }
-            const bool row_ok = n < p.N;
-            bool ok = true;
-            for (int kt = 0; kt < KT; ++kt, ++it) {
-                if ((int)(it & 1) != wg) continue;
-                const int s = it % STAGES, j = it % AST;
-                if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL) ||
-                    !mbar_wait(&aempty[j], ((it / AST) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY)) {
-                    ok = false;
-                    break;
-                }
-                uint32_t r[32];
-                if (kt < p.ktw) {
-                    const int k0 = kt * BK;
-                    const int g0 = k0 / p.gs, g1 = (k0 + 32) / p.gs;
-                    uint32_t s0 = 0, b0 = 0, s1 = 0, b1 = 0;  // bf16x2 broadcast pairs
-                    if (row_ok) {
-                        const uint16_t *sp = reinterpret_cast<const uint16_t *>(sc) + (int64_t)n * p.G;
-                        const uint16_t *bp = reinterpret_cast<const uint16_t *>(bi) + (int64_t)n * p.G;
-                        if (g0 < p.G) {
-                            s0 = sp[g0] * 0x10001u;
-                            b0 = bp[g0] * 0x10001u;
-                        }
-                        if (g1 < p.G) {
-                            s1 = sp[g1] * 0x10001u;
-                            b1 = bp[g1] * 0x10001u;
-                        }
-                    }
-                    const uint8_t *wrow = smem + C::SMEM_W + s * C::W_STAGE_BYTES + row * C::W_ROW_BYTES;
-                    if constexpr (BITS == 4) {
-                        uint4 a = reinterpret_cast<const uint4 *>(wrow)[0];
-                        uint4 b = reinterpret_cast<const uint4 *>(wrow)[1];
-                        const uint32_t wv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            sc = reinterpret_cast<const uint16_t *>(p.scales);
+            bi = reinterpret_cast<const uint16_t *>(p.biases);
+            return wt * BW + row;
+        };
+        // scale/bias bf16 bits of step `it`: {s(group of k0), b(..), s(group of k0+32), b(..)}
+        auto load_sb = [&](uint32_t it, uint32_t out[4]) {
+            out[0] = out[1] = out[2] = out[3] = 0;
+            if (it >= total) return;
+            const int lt = (int)(it / (uint32_t)KT), kt = (int)(it - (uint32_t)lt * KT);
+            if (kt >= p.ktw) return;
+            const uint16_t *sc, *bi;
+            const int n = row_of((int)blockIdx.x + lt * (int)gridDim.x, sc, bi);
+            if (n >= p.N) return;
+            const int g0 = kt * BK / p.gs, g1 = (kt * BK + 32) / p.gs;
+            const int64_t base = (int64_t)n * p.G;
+            if (g0 < p.G) {
+                out[0] = __ldg(sc + base + g0);
+                out[1] = __ldg(bi + base + g0);
+            }
+            if (g1 < p.G) {
+                out[2] = __ldg(sc + base + g1);
+                out[3] = __ldg(bi + base + g1);
+            }
+        };
+        uint32_t sb[4];
+        load_sb((uint32_t)wg, sb);
+        for (uint32_t it = (uint32_t)wg; it < total; it += 2) {
+            uint32_t sb_next[4];
+            load_sb(it + 2, sb_next);
+            const int lt = (int)(it / (uint32_t)KT), kt = (int)(it - (uint32_t)lt * KT);
+            const int s = it % STAGES, j = it % AST;
+            if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL) ||
+                !mbar_wait(&aempty[j], ((it / AST) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY))
+                break;
+            uint32_t r[32];
+            if (kt < p.ktw) {
+                const uint32_t s0 = sb[0] * 0x10001u, b0 = sb[1] * 0x10001u;  // bf16x2 broadcast
+                const uint32_t s1 = sb[2] * 0x10001u, b1 = sb[3] * 0x10001u;
+                const uint8_t *wrow = smem + C::SMEM_W + s * C::W_STAGE_BYTES + row * C::W_ROW_BYTES;
+                if constexpr (BITS == 4) {
+                    uint4 a = reinterpret_cast<const uint4 *>(wrow)[0];
+                    uint4 b = reinterpret_cast<const uint4 *>(wrow)[1];
+                    const uint32_t wv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            uint32_t qp[4];
-                            q4_word_to_bf16_pairs(wv[i], qp);
-                            const uint32_t ss = i < 4 ? s0 : s1, bb = i < 4 ? b0 : b1;
+                    for (int i = 0; i < 8; ++i) {
+                        uint32_t qp[4];
+                        q4_word_to_bf16_pairs(wv[i], qp);
+                        const uint32_t ss = i < 4 ? s0 : s1, bb = i < 4 ? b0 : b1;
 #pragma unroll
-                            for (int t = 0; t < 4; ++t) r[4 * i + t] = hfma2_bf16(qp[t], ss, bb);
-                        }
-                    } else {
-                        const float fs0 = bf16lo(s0), fb0 = bf16lo(b0), fs1 = bf16lo(s1), fb1 = bf16lo(b1);
-#pragma unroll
-                        for (int h = 0; h < 4; ++h) {
-                            uint4 a = reinterpret_cast<const uint4 *>(wrow)[h];
-                            const uint32_t wv[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                const int wi = 4 * h + i;  // word index: codes 4wi..4wi+3
-                                const float ss = wi < 8 ? fs0 : fs1, bb = wi < 8 ? fb0 : fb1;
-                                const float c0 = fmaf(q8_code_f32(wv[i], 0), ss, bb);
-                                const float c1 = fmaf(q8_code_f32(wv[i], 1), ss, bb);
-                                const float c2 = fmaf(q8_code_f32(wv[i], 2), ss, bb);
-                                const float c3 = fmaf(q8_code_f32(wv[i], 3), ss, bb);
-                                r[2 * wi] = pack_bf16x2(c0, c1);
-                                r[2 * wi + 1] = pack_bf16x2(c2, c3);
-                            }
-                        }
+                        for (int t = 0; t < 4; ++t) r[4 * i + t] = hfma2_bf16(qp[t], ss, bb);
                     }
                 } else {
-                    // LoRA step: A = B^T rows for this tile, columns [64l, 64l + 64) of rank.
-                    const int l0 = (kt - p.ktw) * BK;
+                    const float fs0 = bf16lo(s0), fb0 = bf16lo(b0), fs1 = bf16lo(s1), fb1 = bf16lo(b1);
 #pragma unroll
-                    for (int c = 0; c < 32; ++c) {
-                        const int j0 = l0 + 2 * c;
-                        uint32_t lo = 0, hi = 0;
-                        if (row_ok && j0 < p.lora_rank)
-                            lo = reinterpret_cast<const uint16_t *>(p.lora_b)[(int64_t)j0 * p.N + n];
-                        if (row_ok && j0 + 1 < p.lora_rank)
-                            hi = reinterpret_cast<const uint16_t *>(p.lora_b)[(int64_t)(j0 + 1) * p.N + n];
-                        r[c] = lo | (hi << 16);
+                    for (int h = 0; h < 4; ++h) {
+                        uint4 a = reinterpret_cast<const uint4 *>(wrow)[h];
+                        const uint32_t wv[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int wi = 4 * h + i;  // word index: codes 4wi..4wi+3
+                            const float ss = wi < 8 ? fs0 : fs1, bb = wi < 8 ? fb0 : fb1;
+                            const float c0 = fmaf(q8_code_f32(wv[i], 0), ss, bb);
+                            const float c1 = fmaf(q8_code_f32(wv[i], 1), ss, bb);
+                            const float c2 = fmaf(q8_code_f32(wv[i], 2), ss, bb);
+                            const float c3 = fmaf(q8_code_f32(wv[i], 3), ss, bb);
+                            r[2 * wi] = pack_bf16x2(c0, c1);
+                            r[2 * wi + 1] = pack_bf16x2(c2, c3);
+                        }
                     }
                 }
-                tmem_st32(taddr_lane + j * 32, r);
-                tmem_st_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&afull[j]);
-                    mbar_arrive(&empty[s]);
+            } else {
+                // LoRA step: A = B^T rows for this tile, columns [64l, 64l + 64) of rank.
+                const uint16_t *sc, *bi;
+                const int n = row_of((int)blockIdx.x + lt * (int)gridDim.x, sc, bi);
+                const bool row_ok = n < p.N;
+                const int l0 = (kt - p.ktw) * BK;
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const int j0 = l0 + 2 * c;
+                    uint32_t lo = 0, hi = 0;
+                    if (row_ok && j0 < p.lora_rank)
+                        lo = reinterpret_cast<const uint16_t *>(p.lora_b)[(int64_t)j0 * p.N + n];
+                    if (row_ok && j0 + 1 < p.lora_rank)
+                        hi = reinterpret_cast<const uint16_t *>(p.lora_b)[(int64_t)(j0 + 1) * p.N + n];
+                    r[c] = lo | (hi << 16);
                 }
             }
-            if (!ok) break;
+            tmem_st32(taddr_lane + j * 32, r);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&afull[j]);
+                mbar_arrive(&empty[s]);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sb[i] = sb_next[i];
         }
     }
 

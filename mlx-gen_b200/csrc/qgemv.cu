@@ -105,104 +105,167 @@ __device__ __forceinline__ void chunk_mma(float d[4], const uint32_t *wg_words, 
     }
 }
 
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    bytes &= ~15u;  // a hint: rounding down keeps it inside the allocation
+    if (bytes)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Smem layout of x: token g at g * XSTRIDE elements; inside a 128-wide chunk the
+// order is (word i, lane c, element e) so that the four lanes of a row read 64
+// contiguous bytes and the 32-element pad makes two token rows of a quarter-warp
+// fall in different banks.
+__device__ __forceinline__ int xs_index(int k) {
+    const int ch = k >> 7, r = k & 127, c = r >> 5, i = (r >> 3) & 3, e = r & 7;
+    return (ch << 7) + (i << 5) + (c << 3) + e;
+}
+
 template <int BITS, bool SWIGLU>
-__global__ void __launch_bounds__(WARPS * 32) qgemv_kernel(const Params p) {
-    constexpr int LANE_BYTES = 32 * BITS / 8;  // packed bytes per lane per row per chunk
-    constexpr int NW = LANE_BYTES / 4;         // words
-    __shared__ float red[SWIGLU ? 2 : 1][WARPS][16][8];
+__global__ void __launch_bounds__(WARPS * 32, 2) qgemv_kernel(const Params p) {
+    constexpr int NW = BITS;             // packed words per lane per row per chunk (32 codes)
+    constexpr int NPASS = SWIGLU ? 2 : 1;
+    constexpr int U = SWIGLU ? 2 : 4;    // chunks whose loads are in flight together
+    constexpr int PF = 2;                // strips prefetched into L2 ahead of use
+    extern __shared__ __align__(16) uint16_t xs[];
+    __shared__ float red[NPASS][WARPS][16][8];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
-    const int n0 = blockIdx.x * 16;
-    const int rg = min(n0 + g, p.N - 1), rh = min(n0 + g + 8, p.N - 1);  // clamped rows (stores masked)
+    const int nstrips = (p.N + 15) / 16;
     const int64_t wpr = (int64_t)p.K * BITS / 32;  // words per row
     const int nchunks = (p.K + CHUNK - 1) / CHUNK;
+    const int xstride = p.K + 32;
 
-    float d[4] = {0.f, 0.f, 0.f, 0.f}, d2[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int ch = warp; ch < nchunks; ch += WARPS) {
-        // K % 32 == 0, so a lane's 32-code block is all-in or all-out.  Lanes past
-        // K feed zeros (the MMA needs the whole warp converged).
-        const bool kval = ch * CHUNK + 32 * c < p.K;
-        const int k = kval ? ch * CHUNK + 32 * c : 0;
-        const int grp = k / p.gs;
-        // x for token g (zero for padded tokens)
-        uint4 xv[4];
-        if (g < p.M && kval) {
-            const uint4 *xp = reinterpret_cast<const uint4 *>(p.x + (int64_t)g * p.K + k);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) xv[i] = __ldg(xp + i);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) xv[i] = make_uint4(0, 0, 0, 0);
+    // Weights do not depend on the previous kernel: start pulling this CTA's first
+    // strips into L2 before waiting on it (programmatic dependent launch).
+    auto prefetch_strip = [&](int st) {
+        const int r0 = st * 16, rows = min(16, p.N - r0);
+        for (int ps = 0; ps < NPASS; ++ps) {
+            const uint32_t *W = ps ? p.wq2 : p.wq;
+            const uint16_t *S = ps ? p.scales2 : p.scales;
+            const uint16_t *B = ps ? p.biases2 : p.biases;
+            prefetch_l2(W + (int64_t)r0 * wpr, (uint32_t)(rows * wpr * 4));
+            prefetch_l2(S + (int64_t)r0 * p.G, (uint32_t)(rows * p.G * 2));
+            prefetch_l2(B + (int64_t)r0 * p.G, (uint32_t)(rows * p.G * 2));
         }
-#pragma unroll
-        for (int pass = 0; pass < (SWIGLU ? 2 : 1); ++pass) {
-            const uint32_t *W = pass ? p.wq2 : p.wq;
-            const uint16_t *S = pass ? p.scales2 : p.scales;
-            const uint16_t *B = pass ? p.biases2 : p.biases;
-            uint32_t wg_words[NW], wh_words[NW];
-            const uint32_t *pgp = W + rg * wpr + (int64_t)k * BITS / 32;
-            const uint32_t *php = W + rh * wpr + (int64_t)k * BITS / 32;
-#pragma unroll
-            for (int v = 0; v < NW / 4; ++v) {
-                uint4 a = make_uint4(0, 0, 0, 0), b = a;
-                if (kval) {
-                    a = ldg16(pgp + 4 * v);
-                    b = ldg16(php + 4 * v);
-                }
-                wg_words[4 * v] = a.x; wg_words[4 * v + 1] = a.y; wg_words[4 * v + 2] = a.z; wg_words[4 * v + 3] = a.w;
-                wh_words[4 * v] = b.x; wh_words[4 * v + 1] = b.y; wh_words[4 * v + 2] = b.z; wh_words[4 * v + 3] = b.w;
-            }
-            const uint32_t sg = __ldg(S + (int64_t)rg * p.G + grp) * 0x10001u;
-            const uint32_t bg = __ldg(B + (int64_t)rg * p.G + grp) * 0x10001u;
-            const uint32_t sh = __ldg(S + (int64_t)rh * p.G + grp) * 0x10001u;
-            const uint32_t bh = __ldg(B + (int64_t)rh * p.G + grp) * 0x10001u;
-            chunk_mma<BITS>(pass ? d2 : d, wg_words, wh_words, sg, bg, sh, bh, xv);
-        }
+    };
+    if (threadIdx.x < PF) {
+        const int st = blockIdx.x + threadIdx.x * gridDim.x;
+        if (st < nstrips) prefetch_strip(st);
     }
-    // D fragment: d[0],d[1] = (row g, tokens 2c, 2c+1); d[2],d[3] = (row g+8, tokens 2c, 2c+1)
-    red[0][warp][g][2 * c] = d[0];
-    red[0][warp][g][2 * c + 1] = d[1];
-    red[0][warp][g + 8][2 * c] = d[2];
-    red[0][warp][g + 8][2 * c + 1] = d[3];
-    if (SWIGLU) {
-        red[SWIGLU ? 1 : 0][warp][g][2 * c] = d2[0];
-        red[SWIGLU ? 1 : 0][warp][g][2 * c + 1] = d2[1];
-        red[SWIGLU ? 1 : 0][warp][g + 8][2 * c] = d2[2];
-        red[SWIGLU ? 1 : 0][warp][g + 8][2 * c + 1] = d2[3];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    // x -> shared memory (permuted, see xs_index)
+    for (int e = threadIdx.x * 8; e < p.M * p.K; e += WARPS * 32 * 8) {
+        const int m = e / p.K, k = e - m * p.K;
+        *reinterpret_cast<uint4 *>(xs + m * xstride + xs_index(k)) =
+            __ldg(reinterpret_cast<const uint4 *>(p.x + e));
     }
     __syncthreads();
-    if (threadIdx.x < 128) {
-        const int r = threadIdx.x >> 3, m = threadIdx.x & 7;
-        const int n = n0 + r;
-        if (n < p.N && m < p.M) {
-            float acc = 0.f, acc2 = 0.f;
+
+    for (int st = blockIdx.x; st < nstrips; st += gridDim.x) {
+        if (threadIdx.x == 0 && st + PF * (int)gridDim.x < nstrips) prefetch_strip(st + PF * gridDim.x);
+        const int n0 = st * 16;
+        const int rg = min(n0 + g, p.N - 1), rh = min(n0 + g + 8, p.N - 1);  // clamped (stores masked)
+        float d[NPASS][4] = {};
+        for (int cb = warp; cb < nchunks; cb += WARPS * U) {
+            // ---- issue every load of U chunks first
+            uint32_t wgw[U][NPASS][NW], whw[U][NPASS][NW], sbv[U][NPASS][4];
 #pragma unroll
-            for (int w = 0; w < WARPS; ++w) {
-                acc += red[0][w][r][m];
-                if (SWIGLU) acc2 += red[SWIGLU ? 1 : 0][w][r][m];
+            for (int u = 0; u < U; ++u) {
+                const int ch = cb + u * WARPS;
+                const bool kval = ch < nchunks && ch * CHUNK + 32 * c < p.K;
+                const int k = kval ? ch * CHUNK + 32 * c : 0;
+                const int grp = k / p.gs;
+#pragma unroll
+                for (int ps = 0; ps < NPASS; ++ps) {
+                    const uint32_t *W = ps ? p.wq2 : p.wq;
+                    const uint16_t *S = ps ? p.scales2 : p.scales;
+                    const uint16_t *B = ps ? p.biases2 : p.biases;
+                    const uint32_t *pgp = W + rg * wpr + (int64_t)k * BITS / 32;
+                    const uint32_t *php = W + rh * wpr + (int64_t)k * BITS / 32;
+#pragma unroll
+                    for (int v = 0; v < NW / 4; ++v) {
+                        uint4 a = make_uint4(0, 0, 0, 0), b = a;
+                        if (kval) {
+                            a = ldg16(pgp + 4 * v);
+                            b = ldg16(php + 4 * v);
+                        }
+                        wgw[u][ps][4 * v] = a.x; wgw[u][ps][4 * v + 1] = a.y;
+                        wgw[u][ps][4 * v + 2] = a.z; wgw[u][ps][4 * v + 3] = a.w;
+                        whw[u][ps][4 * v] = b.x; whw[u][ps][4 * v + 1] = b.y;
+                        whw[u][ps][4 * v + 2] = b.z; whw[u][ps][4 * v + 3] = b.w;
+                    }
+                    sbv[u][ps][0] = __ldg(S + (int64_t)rg * p.G + grp);
+                    sbv[u][ps][1] = __ldg(B + (int64_t)rg * p.G + grp);
+                    sbv[u][ps][2] = __ldg(S + (int64_t)rh * p.G + grp);
+                    sbv[u][ps][3] = __ldg(B + (int64_t)rh * p.G + grp);
+                }
             }
-            if (p.lora_t) {
-                const __nv_bfloat16 *t = p.lora_t + (int64_t)m * p.rpad;
-                for (int j = 0; j < p.rank; ++j)
-                    acc += __bfloat162float(t[j]) * __bfloat162float(p.lora_b[(int64_t)j * p.N + n]);
+            // ---- then dequantize + MMA
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int ch = cb + u * WARPS;
+                const bool kval = ch < nchunks && ch * CHUNK + 32 * c < p.K;
+                uint4 xv[4];
+                if (g < p.M && kval) {
+                    const uint4 *xp = reinterpret_cast<const uint4 *>(xs + g * xstride + ch * CHUNK + c * 8);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) xv[i] = xp[i * 4];  // word i: +32 elements
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) xv[i] = make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int ps = 0; ps < NPASS; ++ps)
+                    chunk_mma<BITS>(d[ps], wgw[u][ps], whw[u][ps], sbv[u][ps][0] * 0x10001u,
+                                    sbv[u][ps][1] * 0x10001u, sbv[u][ps][2] * 0x10001u,
+                                    sbv[u][ps][3] * 0x10001u, xv);
             }
-            float v = round_bf16(acc);
-            if (p.bias) v = round_bf16(v + __bfloat162float(p.bias[n]));
-            if (SWIGLU) {
-                float u = round_bf16(acc2);
-                if (p.bias2) u = round_bf16(u + __bfloat162float(p.bias2[n]));
-                v = v / (1.0f + __expf(-v)) * u;
-            } else if (p.act == QL_ACT_GELU_TANH) {
-                float t;
-                const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
-                asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(inner));
-                v = 0.5f * v * (1.0f + t);
-            } else if (p.act == QL_ACT_GELU_ERF) {
-                v = 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
-            }
-            p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(v);
         }
+        // D fragment: d[0],d[1] = (row g, tokens 2c, 2c+1); d[2],d[3] = (row g+8, tokens 2c, 2c+1)
+#pragma unroll
+        for (int ps = 0; ps < NPASS; ++ps) {
+            red[ps][warp][g][2 * c] = d[ps][0];
+            red[ps][warp][g][2 * c + 1] = d[ps][1];
+            red[ps][warp][g + 8][2 * c] = d[ps][2];
+            red[ps][warp][g + 8][2 * c + 1] = d[ps][3];
+        }
+        __syncthreads();
+        if (threadIdx.x < 128) {
+            const int r = threadIdx.x >> 3, m = threadIdx.x & 7;
+            const int n = n0 + r;
+            if (n < p.N && m < p.M) {
+                float acc = 0.f, acc2 = 0.f;
+#pragma unroll
+                for (int w = 0; w < WARPS; ++w) {
+                    acc += red[0][w][r][m];
+                    if (SWIGLU) acc2 += red[NPASS - 1][w][r][m];
+                }
+                if (p.lora_t) {
+                    const __nv_bfloat16 *t = p.lora_t + (int64_t)m * p.rpad;
+                    for (int j = 0; j < p.rank; ++j)
+                        acc += __bfloat162float(t[j]) * __bfloat162float(p.lora_b[(int64_t)j * p.N + n]);
+                }
+                float v = round_bf16(acc);
+                if (p.bias) v = round_bf16(v + __bfloat162float(p.bias[n]));
+                if (SWIGLU) {
+                    float u = round_bf16(acc2);
+                    if (p.bias2) u = round_bf16(u + __bfloat162float(p.bias2[n]));
+                    v = v / (1.0f + __expf(-v)) * u;
+                } else if (p.act == QL_ACT_GELU_TANH) {
+                    float t;
+                    const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+                    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(inner));
+                    v = 0.5f * v * (1.0f + t);
+                } else if (p.act == QL_ACT_GELU_ERF) {
+                    v = 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
+                }
+                p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(v);
+            }
+        }
+        __syncthreads();
     }
 }
 
@@ -234,15 +297,33 @@ int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const 
     p.rpad = (int)(rank > 0 ? (rank + 63) / 64 * 64 : 0);
     p.act = act;
     p.y = (__nv_bfloat16 *)y;
-    const int grid = (int)((N + 15) / 16);
+    int dev = 0, sms = 148;
+    QL_CUDA_TRY(cudaGetDevice(&dev));
+    QL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int nstrips = (int)((N + 15) / 16);
+    const size_t smem = (size_t)M * (size_t)(K + 32) * 2;
+    if (smem > 200 * 1024) return fail(QL_EUNSUPPORTED, "GEMV: M*K too large for the x staging buffer");
+    const int per_sm = smem <= 48 * 1024 ? 2 : 1;
+    const int grid = nstrips < per_sm * sms ? nstrips : per_sm * sms;
     const bool sw = act == QL_ACT_SWIGLU;
-    if (bits == 4) {
-        if (sw) qgemv_kernel<4, true><<<grid, WARPS * 32, 0, st>>>(p);
-        else qgemv_kernel<4, false><<<grid, WARPS * 32, 0, st>>>(p);
-    } else {
-        if (sw) qgemv_kernel<8, true><<<grid, WARPS * 32, 0, st>>>(p);
-        else qgemv_kernel<8, false><<<grid, WARPS * 32, 0, st>>>(p);
-    }
+    void (*kfn)(const Params) = bits == 4 ? (sw ? qgemv_kernel<4, true> : qgemv_kernel<4, false>)
+                                          : (sw ? qgemv_kernel<8, true> : qgemv_kernel<8, false>);
+    if (smem > 48 * 1024)
+        QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    // Programmatic dependent launch: the kernel may start (and prefetch its weights)
+    // while the previous kernel on the stream finishes; it waits for that kernel's
+    // results (griddepcontrol.wait) before touching x.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(WARPS * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    QL_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, p));
     QL_CUDA_TRY(cudaGetLastError());
     return QL_OK;
 }

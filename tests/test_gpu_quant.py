@@ -97,11 +97,14 @@ def test_quantize_full_size_roundtrip(dev):
         wq, s, b = qlinear.quantize(w, 64, bits)
         d = qlinear.dequantize(wq, s, b, 64, bits)
         step = s.float().abs().repeat_interleave(64, dim=1)
-        assert torch.all((d.float() - w.float()).abs() <= step * 1.001 + w.float().abs() * 2 ** -7)
+        # one step, plus the bf16 rounding of the stored scale (codes use the fp32 scale) times
+        # the largest code, plus the bf16 rounding of the output
+        slack = 1.001 + (2 ** bits) * 2 ** -8
+        assert torch.all((d.float() - w.float()).abs() <= step * slack + w.float().abs() * 2 ** -7)
         wq2, s2, b2 = qlinear.quantize(d, 64, bits)
         d2 = qlinear.dequantize(wq2, s2, b2, 64, bits)
         step2 = s2.float().abs().repeat_interleave(64, dim=1)
-        assert torch.all((d2.float() - d.float()).abs() <= step2 * 1.001 + d.float().abs() * 2 ** -7)
+        assert torch.all((d2.float() - d.float()).abs() <= step2 * slack + d.float().abs() * 2 ** -7)
         # sampled rows bit-exact against the oracle at full K
         rows = [0, 4095, 13823]
         rq, rs, rb = O.quantize(t2np(w[rows]), 64, bits)
