@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(WARPS * 32, 2) qgemv_kernel(const Params p) {
     const int nstrips = (p.N + 15) / 16;
     const int64_t wpr = (int64_t)p.K * BITS / 32;  // words per row
     const int nchunks = (p.K + CHUNK - 1) / CHUNK;
-    const int xstride = p.K + 32;
+    const int xstride = nchunks * CHUNK + 32;  // whole chunks: the permuted layout fills 128 slots
 
     // Weights do not depend on the previous kernel: start pulling this CTA's first
     // strips into L2 before waiting on it (programmatic dependent launch).
@@ -301,7 +301,7 @@ int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const 
     QL_CUDA_TRY(cudaGetDevice(&dev));
     QL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int nstrips = (int)((N + 15) / 16);
-    const size_t smem = (size_t)M * (size_t)(K + 32) * 2;
+    const size_t smem = (size_t)M * (size_t)((K + CHUNK - 1) / CHUNK * CHUNK + 32) * 2;
     if (smem > 200 * 1024) return fail(QL_EUNSUPPORTED, "GEMV: M*K too large for the x staging buffer");
     const int per_sm = smem <= 48 * 1024 ? 2 : 1;
     const int grid = nstrips < per_sm * sms ? nstrips : per_sm * sms;

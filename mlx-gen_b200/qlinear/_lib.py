@@ -11,7 +11,8 @@ import ctypes as C
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libqlinear.so")
+# QL_LIB_PATH overrides the library location (e.g. an instrumented developer build).
+LIB_PATH = os.environ.get("QL_LIB_PATH") or os.path.join(_HERE, "libqlinear.so")
 
 QL_F32, QL_BF16, QL_F16 = 0, 1, 2
 QL_OK, QL_EINVAL_SHAPE, QL_EUNSUPPORTED, QL_ECUDA, QL_EINVAL_ARG, QL_ETIMEOUT = range(6)

@@ -87,8 +87,9 @@ def test_swiglu_epilogue(dev, kernel, bits):
 @pytest.mark.parametrize("rank", [8, 32, 96])
 def test_lora_epilogue(dev, kernel, rank):
     """LoRA residual scale*(x.A).B fused into the accumulator (src/adapters.rs:260-270).  The
-    reference rounds x.A, (x.A).B, the scale multiply and the sum to bf16 separately; the fused
-    kernel rounds once, so the stated bound is 4 ulps."""
+    reference rounds the base output and the residual to bf16 separately before summing them;
+    where the two cancel, that leaves up to one bf16 ulp of the operands' magnitude, so the
+    stated bound is 4 ulps of the result plus 1/128 of the output scale."""
     M = 7 if kernel == GEMV else 270
     N, K, gs, bits = 256, 384, 64, 4
     rng, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, rank)
@@ -98,7 +99,7 @@ def test_lora_epilogue(dev, kernel, rank):
     y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, bias=np2t(bias, dev),
                                  lora=(np2t(A, dev), np2t(B, dev), 0.75), kernel=kernel)
     ref = O.quantized_matmul(x, wq, s, b, gs, bits, bias=bias, lora_a=A, lora_b=B, lora_scale=0.75)
-    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), ulps=4, what=f"lora r{rank}")
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), ulps=4, atol_frac=2 ** -7, what=f"lora r{rank}")
 
 
 def test_kernels_agree_with_each_other(dev):
