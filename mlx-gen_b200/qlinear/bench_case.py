@@ -1,0 +1,50 @@
+"""One quantized_matmul shape, timed with CUDA events (also the small case used for ncu
+captures).  Usage:
+
+    python -m qlinear.bench_case M N K BITS [ACT|none] [REPS] [gemm|gemv|auto]
+
+(run with mlx-gen_b200 on PYTHONPATH).  Prints time per call and TFLOP/s / GB/s.
+Weights ~N(0, 0.02) bf16 quantized on the device (group 64), x ~N(0, 1), bias ~N(0, 0.02).
+"""
+import sys
+
+import torch
+
+import qlinear
+
+
+def main(argv):
+    M, N, K, bits = (int(v) for v in argv[:4])
+    act = argv[4] if len(argv) > 4 and argv[4] != "none" else None
+    reps = int(argv[5]) if len(argv) > 5 else 20
+    kernel = {"gemm": qlinear.KERNEL_GEMM, "gemv": qlinear.KERNEL_GEMV, "auto": qlinear.KERNEL_AUTO}[
+        argv[6] if len(argv) > 6 else "auto"]
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    bias = (torch.randn(N, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    wq, s, b = qlinear.quantize(w, 64, bits)
+    del w
+    y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+
+    def f():
+        qlinear.quantized_matmul(x, wq, s, b, True, 64, bits, bias=bias, act=act, kernel=kernel, out=y)
+
+    for _ in range(3):
+        f()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        f()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    nbytes = N * K * bits // 8 + N * (K // 64) * 4 + (M * K + M * N) * 2
+    print(f"M={M} N={N} K={K} Q{bits} act={act}: {ms * 1e3:.1f} us  {2 * M * N * K / ms / 1e9:.1f} TFLOP/s  "
+          f"{nbytes / ms / 1e6:.1f} GB/s")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:])
