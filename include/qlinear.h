@@ -128,6 +128,19 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
  * epilogue (0 when none; the LoRA residual needs M * round_up(rank, 64) * 2). */
 size_t ql_matmul_workspace_size(int64_t M, int64_t N, int64_t K, const ql_epilogue *ep);
 
+/* Same as ql_quantized_matmul, for callers that cannot allocate device memory
+ * (allocator hooks, real-time loops that must not enter the driver's allocator,
+ * runtimes whose memory is fully reserved).  No counterpart in the reference.
+ * The LoRA workspace comes from a fixed 8 MiB device array inside the library
+ * (ep->workspace is ignored); a request above that (M * round_up(rank, 64) * 2
+ * bytes) returns QL_EUNSUPPORTED.  The first call on a device looks up the array
+ * with that device current -- make it before any stream capture.  Calls share the
+ * array: calls that overlap on the GPU race.  Allocates nothing. */
+int ql_quantized_matmul_noalloc(const void *x, int x_dtype, int64_t M, int64_t K,
+                                const uint32_t *wq, const void *scales, const void *biases,
+                                int sb_dtype, int64_t N, int group_size, int bits, int transpose,
+                                const ql_epilogue *ep, void *y, int y_dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

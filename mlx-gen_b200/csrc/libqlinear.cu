@@ -8,3 +8,4 @@
 #include "qgemv.cu"
 #include "qmm_generic.cu"
 #include "quantize.cu"
+#include "noalloc.cu"
