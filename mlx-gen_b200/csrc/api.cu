@@ -38,7 +38,7 @@ int launch_qgemv(const void *, int64_t, int64_t, const uint32_t *, const void *,
                  const void *, int, const void *, const void *, int64_t, void *, cudaStream_t);
 int launch_qgemm_sm100(const void *, int64_t, int64_t, const uint32_t *, const void *, const void *,
                        const uint32_t *, const void *, const void *, int64_t, int, int, const void *,
-                       const void *, int, const void *, const void *, int64_t, void *, cudaStream_t);
+                       const void *, int, const void *, const void *, int64_t, void *, int, cudaStream_t);
 int launch_qmm_generic(const void *, int, int64_t, int64_t, const uint32_t *, const void *,
                        const void *, const uint32_t *, const void *, const void *, int, int64_t, int,
                        int, const void *, const void *, int, const void *, const void *, int64_t,
@@ -169,7 +169,7 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
     if (kernel != QL_KERNEL_GENERIC && !tc_dtypes)
         return fail(QL_EUNSUPPORTED, "tensor-core kernels need bf16 x, scales and y");
     if (kernel == QL_KERNEL_GEMV && M > 8) return fail(QL_EUNSUPPORTED, "GEMV kernel needs M <= 8");
-    if (kernel < QL_KERNEL_AUTO || kernel > QL_KERNEL_GEMM) return fail(QL_EINVAL_ARG, "unknown kernel %d", kernel);
+    if (kernel < QL_KERNEL_AUTO || kernel > QL_KERNEL_GEMM_1SM) return fail(QL_EINVAL_ARG, "unknown kernel %d", kernel);
 
     if (kernel == QL_KERNEL_GENERIC)
         return launch_qmm_generic(x, x_dtype, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up,
@@ -190,7 +190,8 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
         return launch_qgemv(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size,
                             bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y, st);
     return launch_qgemm_sm100(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size,
-                              bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y, st);
+                              bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y,
+                              kernel == QL_KERNEL_GEMM_1SM ? 1 : 2, st);
 }
 
 }  // extern "C"

@@ -34,28 +34,32 @@ namespace ql {
 namespace gemm {
 
 constexpr int BT = 256;        // tokens per tile (MMA N)
-constexpr int BW = 128;        // weight rows per tile (MMA M)
+constexpr int BW = 128;        // weight rows per CTA per tile (MMA M per CTA)
 constexpr int BK = 64;         // K per pipeline step (one 128-byte swizzle row of bf16)
-constexpr int STAGES = 5;      // smem ring depth
 constexpr int AST = 4;         // TMEM A ring depth (32 columns each)
 constexpr int NTHREADS = 512;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t ACC_COL = 0;
 constexpr uint32_t A_COL = 256;
 constexpr uint32_t STG_COL = 384;   // bf16 staging of the finished tile (128 columns)
-constexpr int X_STAGE_BYTES = BT * BK * 2;  // 32 KB
 
-template <int BITS>
+// CG = CTAs per MMA: 1 (cta_group::1, 128 x 256 tile per CTA) or 2 (a CTA pair runs
+// cta_group::2 MMAs on a 256 x 256 tile; each CTA holds 128 weight rows in its TMEM and
+// stages 128 of the 256 tokens in its smem, which halves the x traffic per SM).
+template <int BITS, int CG>
 struct Cfg {
-    static constexpr int W_ROW_BYTES = BK * BITS / 8;           // 32 (Q4) / 64 (Q8)
-    static constexpr int W_STAGE_BYTES = BW * W_ROW_BYTES;      // 4 KB / 8 KB
-    static constexpr int W_BOX_WORDS = BK * BITS / 32;          // 8 / 16
+    static constexpr int STAGES = CG == 1 ? 5 : (BITS == 4 ? 8 : 7);  // smem ring depth
+    static constexpr int XROWS = BT / CG;                          // tokens staged per CTA
+    static constexpr int X_STAGE_BYTES = XROWS * BK * 2;           // 32 KB / 16 KB
+    static constexpr int W_ROW_BYTES = BK * BITS / 8;              // 32 (Q4) / 64 (Q8)
+    static constexpr int W_STAGE_BYTES = BW * W_ROW_BYTES;         // 4 KB / 8 KB
+    static constexpr int W_BOX_WORDS = BK * BITS / 32;             // 8 / 16
     static constexpr int SMEM_X = 0;
     static constexpr int SMEM_W = SMEM_X + STAGES * X_STAGE_BYTES;
     static constexpr int SMEM_XCH = SMEM_W + STAGES * W_STAGE_BYTES;  // swiglu exchange
     static constexpr int XCH_BYTES = 64 * 33 * 4;
     static constexpr int SMEM_BAR = SMEM_XCH + XCH_BYTES;
-    static constexpr int NBAR = 2 * STAGES + 2 * AST + 2;
+    static constexpr int NBAR = 3 * STAGES + 2 * AST + 2;
     static constexpr int SMEM_MISC = SMEM_BAR + NBAR * 8;
     static constexpr int SMEM_TOTAL = SMEM_MISC + 16 + 1024;  // + alignment slack
 };
@@ -89,41 +93,50 @@ __device__ __forceinline__ float gelu_erf_f(float x) {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
-
-template <int BITS, bool SWIGLU>
+template <int BITS, bool SWIGLU, int CG>
 __global__ void __launch_bounds__(NTHREADS, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                  const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_t,
                  const Params p) {
-    using C = Cfg<BITS>;
+    using C = Cfg<BITS, CG>;
+    constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::SMEM_BAR);
-    uint64_t *full = bars;
-    uint64_t *empty = bars + STAGES;
-    uint64_t *afull = bars + 2 * STAGES;
-    uint64_t *aempty = afull + AST;
-    uint64_t *accfull = aempty + AST;
-    uint64_t *accempty = accfull + 1;
+    uint64_t *xfull = bars;                 // x halves landed (used in the leader CTA)
+    uint64_t *wfull = bars + STAGES;        // packed W landed (local)
+    uint64_t *empty = bars + 2 * STAGES;    // stage free: MMA done + local dequant done
+    uint64_t *afull = bars + 3 * STAGES;    // TMEM A slot written (leader: both CTAs' warps)
+    uint64_t *aempty = afull + AST;         // TMEM A slot consumed by the MMA
+    uint64_t *accfull = aempty + AST;       // accumulator complete
+    uint64_t *accempty = accfull + 1;       // accumulator drained (leader: both CTAs' warps)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::SMEM_MISC);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::SMEM_MISC + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = CG == 2 ? cluster_ctarank() : 0;
+    const int cid = (int)blockIdx.x / CG, ncl = (int)gridDim.x / CG;
     const int num_tiles = p.num_w_tiles * p.num_t_tiles;
     const int KT = p.ktw + p.ktl;
+    // shared::cluster addresses in the leader CTA (rank 0) / of the peer's abort flag
+    auto leader = [&](const void *local) -> uint32_t {
+        return CG == 2 ? mapa_shared(smem_u32(local), 0) : smem_u32(local);
+    };
+    const uint32_t peer_abort = CG == 2 ? mapa_shared(smem_u32((const void *)abort_flag), rank ^ 1) : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1 + 4);  // MMA commit + 4 dequant warps
+            mbar_init(&xfull[s], 1);
+            mbar_init(&wfull[s], 1);
+            mbar_init(&empty[s], 1 + 4);  // MMA commit + 4 local dequant warps
         }
         for (int j = 0; j < AST; ++j) {
-            mbar_init(&afull[j], 4);
+            mbar_init(&afull[j], 4 * CG);
             mbar_init(&aempty[j], 1);
         }
         mbar_init(accfull, 1);
-        mbar_init(accempty, 4);
+        mbar_init(accempty, 4 * CG);
         *abort_flag = 0;
         mbar_fence_init();
         prefetch_tmap(&tm_x);
@@ -131,9 +144,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (SWIGLU) prefetch_tmap(&tm_w2);
         if (p.ktl) prefetch_tmap(&tm_t);
     }
-    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    if (warp == 1) {
+        if (CG == 2) tmem_alloc_pair(tmem_slot, TMEM_COLS);
+        else tmem_alloc(tmem_slot, TMEM_COLS);
+    }
     tc_fence_before();
-    __syncthreads();
+    if (CG == 2) cluster_sync_all();  // peer barriers initialised before any remote arrive
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -141,59 +158,83 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // ---------------------------------------------------------------- TMA producer
         if (lane == 0) {
             uint32_t it = 0;
-            for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+            for (int tile = cid; tile < num_tiles && !*abort_flag; tile += ncl) {
                 const int wt = tile % p.num_w_tiles, tt = tile / p.num_w_tiles;
+                const int xrow = tt * BT + (int)rank * C::XROWS;
                 for (int kt = 0; kt < KT; ++kt, ++it) {
                     const int s = it % STAGES;
-                    if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY))
+                    if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY,
+                                   peer_abort))
                         break;
-                    uint8_t *xs = smem + C::SMEM_X + s * X_STAGE_BYTES;
+                    uint8_t *xs = smem + C::SMEM_X + s * C::X_STAGE_BYTES;
                     uint8_t *ws = smem + C::SMEM_W + s * C::W_STAGE_BYTES;
-                    if (kt < p.ktw) {
-                        mbar_arrive_expect_tx(&full[s], X_STAGE_BYTES + C::W_STAGE_BYTES);
-                        tma_load_2d(xs, &tm_x, &full[s], kt * BK, tt * BT);
+                    const bool wstep = kt < p.ktw;
+                    // x half (or LoRA T half): counted on the leader's xfull[s]
+                    if (rank == 0) mbar_arrive_expect_tx(&xfull[s], CG * C::X_STAGE_BYTES);
+                    const CUtensorMap *xm = wstep ? &tm_x : &tm_t;
+                    const int xk = wstep ? kt * BK : (kt - p.ktw) * BK;
+                    if (CG == 2) tma_load_2d_pair(xs, xm, leader(&xfull[s]), xk, xrow);
+                    else tma_load_2d(xs, xm, &xfull[s], xk, xrow);
+                    // packed W rows of this CTA: counted on the local wfull[s]
+                    if (wstep) {
+                        mbar_arrive_expect_tx(&wfull[s], C::W_STAGE_BYTES);
                         if (SWIGLU) {
-                            tma_load_2d(ws, &tm_w, &full[s], kt * C::W_BOX_WORDS, wt * 64);
-                            tma_load_2d(ws + 64 * C::W_ROW_BYTES, &tm_w2, &full[s], kt * C::W_BOX_WORDS,
-                                        wt * 64);
+                            const int r0 = (wt * CG + (int)rank) * 64;
+                            tma_load_2d(ws, &tm_w, &wfull[s], kt * C::W_BOX_WORDS, r0);
+                            tma_load_2d(ws + 64 * C::W_ROW_BYTES, &tm_w2, &wfull[s], kt * C::W_BOX_WORDS, r0);
                         } else {
-                            tma_load_2d(ws, &tm_w, &full[s], kt * C::W_BOX_WORDS, wt * BW);
+                            tma_load_2d(ws, &tm_w, &wfull[s], kt * C::W_BOX_WORDS, (wt * CG + (int)rank) * BW);
                         }
                     } else {
-                        mbar_arrive_expect_tx(&full[s], X_STAGE_BYTES);
-                        tma_load_2d(xs, &tm_t, &full[s], (kt - p.ktw) * BK, tt * BT);
+                        mbar_arrive(&wfull[s]);  // nothing to load; keep the phase moving
                     }
                 }
             }
         }
     } else if (warp == 1) {
-        // ---------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_bf16(BW, BT);
+        // ---------------------------------------------------------------- MMA issuer (leader CTA)
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16(BW * CG, BT);
             uint32_t it = 0, tcount = 0;
-            for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++tcount) {
-                if (!mbar_wait(accempty, (tcount & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_ACC)) break;
+            for (int tile = cid; tile < num_tiles && !*abort_flag; tile += ncl, ++tcount) {
+                if (!mbar_wait(accempty, (tcount & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_ACC, peer_abort)) break;
                 tc_fence_after();
                 bool ok = true;
                 for (int kt = 0; kt < KT; ++kt, ++it) {
                     const int s = it % STAGES, j = it % AST;
-                    if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL) ||
-                        !mbar_wait(&afull[j], (it / AST) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL)) {
+                    if (!mbar_wait(&xfull[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort) ||
+                        !mbar_wait(&afull[j], (it / AST) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t bdesc =
-                        umma_desc_k_sw128(smem_u32(smem + C::SMEM_X + s * X_STAGE_BYTES));
+                    const uint64_t bdesc = umma_desc_k_sw128(smem_u32(smem + C::SMEM_X + s * C::X_STAGE_BYTES));
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk)
-                        tc_mma_ts(tmem + ACC_COL, tmem + A_COL + j * 32 + kk * 8, bdesc + 2 * kk, idesc,
-                                  (kt | kk) != 0);
-                    tc_commit(&empty[s]);
-                    tc_commit(&aempty[j]);
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        if (CG == 2)
+                            tc_mma_ts_pair(tmem + ACC_COL, tmem + A_COL + j * 32 + kk * 8, bdesc + 2 * kk, idesc,
+                                           (kt | kk) != 0);
+                        else
+                            tc_mma_ts(tmem + ACC_COL, tmem + A_COL + j * 32 + kk * 8, bdesc + 2 * kk, idesc,
+                                      (kt | kk) != 0);
+                    }
+                    if (CG == 2) {  // signal both CTAs of the pair
+                        tc_commit_pair(smem_u32(&empty[s]));
+                        tc_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));
+                        tc_commit_pair(smem_u32(&aempty[j]));
+                        tc_commit_pair(mapa_shared(smem_u32(&aempty[j]), 1));
+                    } else {
+                        tc_commit(&empty[s]);
+                        tc_commit(&aempty[j]);
+                    }
                 }
                 if (!ok) break;
-                tc_commit(accfull);
+                if (CG == 2) {
+                    tc_commit_pair(smem_u32(accfull));
+                    tc_commit_pair(mapa_shared(smem_u32(accfull), 1));
+                } else {
+                    tc_commit(accfull);
+                }
             }
         }
     } else if (warp >= 4 && warp < 8) {
@@ -201,28 +242,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // Phase 1 drains the fp32 accumulator as fast as possible: each 32-column
         // chunk is rounded (+ bias, rounded again: the reference's two roundings) and
         // packed to bf16 pairs into the free TMEM columns [STG_COL, STG_COL + 128),
-        // then the accumulator is released so the MMA warp can start the next tile.
+        // then the accumulator is released so the MMA can start the next tile.
         // Phase 2 reads the staged bf16 values back, applies the activation and
         // writes y with warp-coalesced stores (32 lanes = 32 consecutive columns).
         const int q = warp & 3;
-        const int row = q * 32 + lane;  // TMEM lane == weight row within the tile
+        const int row = q * 32 + lane;  // TMEM lane == weight row within this CTA's half
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+        const uint32_t accempty_leader = leader(accempty);
         float *xch = reinterpret_cast<float *>(smem + C::SMEM_XCH);
         uint32_t tcount = 0;
-        for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++tcount) {
+        for (int tile = cid; tile < num_tiles && !*abort_flag; tile += ncl, ++tcount) {
             const int wt = tile % p.num_w_tiles, tt = tile / p.num_w_tiles;
             int n;
             const __nv_bfloat16 *bp;
             if (SWIGLU) {
-                n = wt * 64 + (row & 63);
+                n = (wt * CG + (int)rank) * 64 + (row & 63);
                 bp = row < 64 ? p.bias : p.bias2;
             } else {
-                n = wt * BW + row;
+                n = (wt * CG + (int)rank) * BW + row;
                 bp = p.bias;
             }
             const bool has_bias = bp != nullptr;
             const float bias = (has_bias && n < p.N) ? __bfloat162float(bp[n]) : 0.f;
-            if (!mbar_wait(accfull, tcount & 1, abort_flag, DEV_ERR_TIMEOUT_ACC)) break;
+            if (!mbar_wait(accfull, tcount & 1, abort_flag, DEV_ERR_TIMEOUT_ACC, peer_abort)) break;
             tc_fence_after();
 #pragma unroll 1
             for (int c = 0; c < BT / 32; ++c) {
@@ -244,7 +286,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(accempty);  // accumulator free for the next tile
+            if (lane == 0) mbar_arrive_cluster(accempty_leader);  // accumulator free for the next tile
 
             const int m0 = tt * BT;
 #pragma unroll 1
@@ -291,7 +333,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int wg = (warp - 8) >> 2, q = warp & 3;
         const int row = q * 32 + lane;
         const uint32_t taddr_lane = tmem + ((uint32_t)(q * 32) << 16) + A_COL;
-        const int my_tiles = (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        const int my_tiles = cid < num_tiles ? (num_tiles - 1 - cid) / ncl + 1 : 0;
         const uint32_t total = (uint32_t)my_tiles * (uint32_t)KT;
 
         // weight row (global) of this thread for tile `tile`, plus its scale/bias arrays
@@ -300,11 +342,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (SWIGLU) {
                 sc = reinterpret_cast<const uint16_t *>(row < 64 ? p.scales : p.scales2);
                 bi = reinterpret_cast<const uint16_t *>(row < 64 ? p.biases : p.biases2);
-                return wt * 64 + (row & 63);
+                return (wt * CG + (int)rank) * 64 + (row & 63);
             }
             sc = reinterpret_cast<const uint16_t *>(p.scales);
             bi = reinterpret_cast<const uint16_t *>(p.biases);
-            return wt * BW + row;
+            return (wt * CG + (int)rank) * BW + row;
         };
         // scale/bias bf16 bits of step `it`: {s(group of k0), b(..), s(group of k0+32), b(..)}
         auto load_sb = [&](uint32_t it, uint32_t out[4]) {
@@ -313,7 +355,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int lt = (int)(it / (uint32_t)KT), kt = (int)(it - (uint32_t)lt * KT);
             if (kt >= p.ktw) return;
             const uint16_t *sc, *bi;
-            const int n = row_of((int)blockIdx.x + lt * (int)gridDim.x, sc, bi);
+            const int n = row_of(cid + lt * ncl, sc, bi);
             if (n >= p.N) return;
             const int g0 = kt * BK / p.gs, g1 = (kt * BK + 32) / p.gs;
             const int64_t base = (int64_t)n * p.G;
@@ -333,8 +375,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             load_sb(it + 2, sb_next);
             const int lt = (int)(it / (uint32_t)KT), kt = (int)(it - (uint32_t)lt * KT);
             const int s = it % STAGES, j = it % AST;
-            if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL) ||
-                !mbar_wait(&aempty[j], ((it / AST) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY))
+            if (!mbar_wait(&wfull[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort) ||
+                !mbar_wait(&aempty[j], ((it / AST) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY, peer_abort))
                 break;
             uint32_t r[32];
             if (kt < p.ktw) {
@@ -375,7 +417,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             } else {
                 // LoRA step: A = B^T rows for this tile, columns [64l, 64l + 64) of rank.
                 const uint16_t *sc, *bi;
-                const int n = row_of((int)blockIdx.x + lt * (int)gridDim.x, sc, bi);
+                const int n = row_of(cid + lt * ncl, sc, bi);
                 const bool row_ok = n < p.N;
                 const int l0 = (kt - p.ktw) * BK;
 #pragma unroll
@@ -394,7 +436,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&afull[j]);
+                mbar_arrive_cluster(leader(&afull[j]));
                 mbar_arrive(&empty[s]);
             }
 #pragma unroll
@@ -403,10 +445,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 
     tc_fence_before();
-    __syncthreads();
+    // no CTA of a pair may exit while its peer can still signal its barriers
+    if (CG == 2) cluster_sync_all();
+    else __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, TMEM_COLS);
+        if (CG == 2) tmem_dealloc_pair(tmem, TMEM_COLS);
+        else tmem_dealloc(tmem, TMEM_COLS);
     }
 }
 
@@ -446,23 +491,44 @@ static int make_map_2d(CUtensorMap *map, CUtensorMapDataType dt, int elem_bytes,
     return QL_OK;
 }
 
-template <int BITS, bool SWIGLU>
+template <int BITS, bool SWIGLU, int CG>
 static int launch_t(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mw2,
                     const CUtensorMap &mt, const Params &p, cudaStream_t st) {
-    using C = Cfg<BITS>;
-    auto kfn = qgemm_kernel<BITS, SWIGLU>;
+    using C = Cfg<BITS, CG>;
+    auto kfn = qgemm_kernel<BITS, SWIGLU, CG>;
     static bool configured = false;  // per template instance; attribute is per-function
     if (!configured) {
         QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_TOTAL));
+        if (CG == 2) QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         configured = true;
     }
     int dev = 0, sms = 148;
     QL_CUDA_TRY(cudaGetDevice(&dev));
     QL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int tiles = p.num_w_tiles * p.num_t_tiles;
-    const int grid = tiles < sms ? tiles : sms;
-    kfn<<<grid, NTHREADS, C::SMEM_TOTAL, st>>>(mx, mw, mw2, mt, p);
-    QL_CUDA_TRY(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = C::SMEM_TOTAL;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CG;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // persistent grid: as many clusters as can be resident at once (pairs need two free
+    // SMs of one GPC), never more than there are tiles
+    static int max_clusters = 0;
+    if (!max_clusters) {
+        cfg.gridDim = dim3((unsigned)((sms / CG) * CG));
+        int mc = 0;
+        if (CG == 1 || cudaOccupancyMaxActiveClusters(&mc, kfn, &cfg) != cudaSuccess || mc <= 0) mc = sms / CG;
+        max_clusters = mc;
+    }
+    const int clusters = tiles < max_clusters ? tiles : max_clusters;
+    cfg.gridDim = dim3((unsigned)(clusters * CG));
+    QL_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, mx, mw, mw2, mt, p));
     return QL_OK;
 }
 
@@ -474,9 +540,10 @@ int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, 
                        const void *biases, const uint32_t *wq2, const void *scales2,
                        const void *biases2, int64_t N, int gs, int bits, const void *bias,
                        const void *bias2, int act, const void *lora_t, const void *lora_b,
-                       int64_t rank, void *y, cudaStream_t st) {
+                       int64_t rank, void *y, int cg, cudaStream_t st) {
     using namespace gemm;
     const bool swiglu = act == QL_ACT_SWIGLU;
+    const int wrows = (swiglu ? 64 : BW) * cg;  // output columns per tile
     Params p{};
     p.M = (int)M;
     p.N = (int)N;
@@ -487,7 +554,7 @@ int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, 
     const int64_t rpad = rank > 0 ? (rank + BK - 1) / BK * BK : 0;
     p.ktl = (int)(rpad / BK);
     p.act = act;
-    p.num_w_tiles = (int)((N + (swiglu ? 64 : BW) - 1) / (swiglu ? 64 : BW));
+    p.num_w_tiles = (int)((N + wrows - 1) / wrows);
     p.num_t_tiles = (int)((M + BT - 1) / BT);
     p.scales = (const __nv_bfloat16 *)scales;
     p.biases = (const __nv_bfloat16 *)biases;
@@ -500,8 +567,9 @@ int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, 
     p.y = (__nv_bfloat16 *)y;
 
     CUtensorMap mx, mw, mw2, mt;
+    const uint32_t xbox = (uint32_t)(BT / cg);
     int rc = make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, (uint64_t)K, (uint64_t)M,
-                         (uint64_t)K * 2, BK, BT, CU_TENSOR_MAP_SWIZZLE_128B);
+                         (uint64_t)K * 2, BK, xbox, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     const uint64_t words = (uint64_t)K * bits / 32;
     const uint32_t box_words = (uint32_t)(BK * bits / 32);
@@ -518,12 +586,17 @@ int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, 
     mt = mx;
     if (rpad) {
         rc = make_map_2d(&mt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, lora_t, (uint64_t)rpad, (uint64_t)M,
-                         (uint64_t)rpad * 2, BK, BT, CU_TENSOR_MAP_SWIZZLE_128B);
+                         (uint64_t)rpad * 2, BK, xbox, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
+    if (cg == 2) {
+        if (bits == 4)
+            return swiglu ? launch_t<4, true, 2>(mx, mw, mw2, mt, p, st) : launch_t<4, false, 2>(mx, mw, mw2, mt, p, st);
+        return swiglu ? launch_t<8, true, 2>(mx, mw, mw2, mt, p, st) : launch_t<8, false, 2>(mx, mw, mw2, mt, p, st);
+    }
     if (bits == 4)
-        return swiglu ? launch_t<4, true>(mx, mw, mw2, mt, p, st) : launch_t<4, false>(mx, mw, mw2, mt, p, st);
-    return swiglu ? launch_t<8, true>(mx, mw, mw2, mt, p, st) : launch_t<8, false>(mx, mw, mw2, mt, p, st);
+        return swiglu ? launch_t<4, true, 1>(mx, mw, mw2, mt, p, st) : launch_t<4, false, 1>(mx, mw, mw2, mt, p, st);
+    return swiglu ? launch_t<8, true, 1>(mx, mw, mw2, mt, p, st) : launch_t<8, false, 1>(mx, mw, mw2, mt, p, st);
 }
 
 }  // namespace ql
