@@ -56,8 +56,8 @@ typedef enum {
     QL_KERNEL_AUTO = 0,    /* GEMV for M <= 8, tcgen05 GEMM otherwise (bf16)    */
     QL_KERNEL_GENERIC = 1, /* CUDA-core fp32 kernel; any dtype                   */
     QL_KERNEL_GEMV = 2,    /* M <= 8, bf16 x and bf16 scales                     */
-    QL_KERNEL_GEMM = 3,    /* tcgen05 / TMEM GEMM on CTA pairs (cta_group::2)    */
-    QL_KERNEL_GEMM_1SM = 4, /* the same GEMM with one CTA per MMA (cta_group::1)  */
+    QL_KERNEL_GEMM = 3,    /* tcgen05 / TMEM GEMM, one CTA per MMA (cta_group::1) */
+    QL_KERNEL_GEMM_PAIR = 4, /* the same GEMM on CTA pairs (cta_group::2); slower today */
 } ql_kernel;
 
 /* Fused epilogue and options of ql_quantized_matmul.  Zero-initialise, then set

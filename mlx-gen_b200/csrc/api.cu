@@ -169,7 +169,7 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
     if (kernel != QL_KERNEL_GENERIC && !tc_dtypes)
         return fail(QL_EUNSUPPORTED, "tensor-core kernels need bf16 x, scales and y");
     if (kernel == QL_KERNEL_GEMV && M > 8) return fail(QL_EUNSUPPORTED, "GEMV kernel needs M <= 8");
-    if (kernel < QL_KERNEL_AUTO || kernel > QL_KERNEL_GEMM_1SM) return fail(QL_EINVAL_ARG, "unknown kernel %d", kernel);
+    if (kernel < QL_KERNEL_AUTO || kernel > QL_KERNEL_GEMM_PAIR) return fail(QL_EINVAL_ARG, "unknown kernel %d", kernel);
 
     if (kernel == QL_KERNEL_GENERIC)
         return launch_qmm_generic(x, x_dtype, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up,
@@ -191,7 +191,7 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
                             bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y, st);
     return launch_qgemm_sm100(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size,
                               bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y,
-                              kernel == QL_KERNEL_GEMM_1SM ? 1 : 2, st);
+                              kernel == QL_KERNEL_GEMM_PAIR ? 2 : 1, st);
 }
 
 }  // extern "C"

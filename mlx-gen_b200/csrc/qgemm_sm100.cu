@@ -27,11 +27,32 @@
 //     64 rows of W3 (up) in lanes 64-127; the epilogue pairs them through smem.
 //   * Every mbarrier wait is bounded (ql_common.cuh mbar_wait); on timeout the
 //     kernel records an error, every role drains, and TMEM is freed.
+#include <stdio.h>
+#include <stdlib.h>
+
 #include "ql_common.cuh"
 
 namespace ql {
 
 namespace gemm {
+
+#ifdef QL_TRACE
+// Developer instrumentation (built only with -DQL_TRACE): per-CTA cycle counters of each
+// role's waits, read back with ql_debug_trace().
+__device__ unsigned long long g_trace[16][160];
+#define TR_WAIT(slot, expr)                                                   \
+    ({                                                                        \
+        const long long _t0 = clock64();                                      \
+        const bool _ok = (expr);                                              \
+        if (lane == 0) atomicAdd(&g_trace[slot][blockIdx.x % 160], clock64() - _t0); \
+        _ok;                                                                  \
+    })
+#else
+#define TR_WAIT(slot, expr) (expr)
+#endif
+#ifndef QL_SB_AHEAD
+#define QL_SB_AHEAD 3
+#endif
 
 constexpr int BT = 256;        // tokens per tile (MMA N)
 constexpr int BW = 128;        // weight rows per CTA per tile (MMA M per CTA)
@@ -153,6 +174,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+#ifdef QL_TRACE
+    if (threadIdx.x == 32) g_trace[7][blockIdx.x % 160] -= clock64();
+#endif
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
@@ -163,8 +187,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const int xrow = tt * BT + (int)rank * C::XROWS;
                 for (int kt = 0; kt < KT; ++kt, ++it) {
                     const int s = it % STAGES;
-                    if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY,
-                                   peer_abort))
+                    if (!TR_WAIT(0, mbar_wait<CG == 2>(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY,
+                                   peer_abort)))
                         break;
                     uint8_t *xs = smem + C::SMEM_X + s * C::X_STAGE_BYTES;
                     uint8_t *ws = smem + C::SMEM_W + s * C::W_STAGE_BYTES;
@@ -197,13 +221,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             constexpr uint32_t idesc = umma_idesc_bf16(BW * CG, BT);
             uint32_t it = 0, tcount = 0;
             for (int tile = cid; tile < num_tiles && !*abort_flag; tile += ncl, ++tcount) {
-                if (!mbar_wait(accempty, (tcount & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_ACC, peer_abort)) break;
+                if (!TR_WAIT(1, mbar_wait<CG == 2>(accempty, (tcount & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_ACC, peer_abort))) break;
                 tc_fence_after();
                 bool ok = true;
                 for (int kt = 0; kt < KT; ++kt, ++it) {
                     const int s = it % STAGES, j = it % AST;
-                    if (!mbar_wait(&xfull[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort) ||
-                        !mbar_wait(&afull[j], (it / AST) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort)) {
+                    if (!TR_WAIT(2, mbar_wait<CG == 2>(&xfull[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort)) ||
+                        !TR_WAIT(3, mbar_wait<CG == 2>(&afull[j], (it / AST) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort))) {
                         ok = false;
                         break;
                     }
@@ -264,7 +288,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             const bool has_bias = bp != nullptr;
             const float bias = (has_bias && n < p.N) ? __bfloat162float(bp[n]) : 0.f;
-            if (!mbar_wait(accfull, tcount & 1, abort_flag, DEV_ERR_TIMEOUT_ACC, peer_abort)) break;
+            if (!TR_WAIT(warp == 4 ? 4 : 15, mbar_wait<CG == 2>(accfull, tcount & 1, abort_flag, DEV_ERR_TIMEOUT_ACC, peer_abort))) break;
             tc_fence_after();
 #pragma unroll 1
             for (int c = 0; c < BT / 32; ++c) {
@@ -286,7 +310,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(accempty_leader);  // accumulator free for the next tile
+            if (lane == 0) {  // accumulator free for the next tile
+                if (CG == 2 && rank != 0) mbar_arrive_cluster(accempty_leader);
+                else mbar_arrive(accempty);
+            }
 
             const int m0 = tt * BT;
 #pragma unroll 1
@@ -368,17 +395,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 out[3] = __ldg(bi + base + g1);
             }
         };
-        uint32_t sb[4];
-        load_sb((uint32_t)wg, sb);
+        // scales/biases are loaded QL_SB_AHEAD of this warpgroup's steps ahead of use
+        constexpr int AHEAD = QL_SB_AHEAD;
+        uint32_t sbq[AHEAD][4];
+#pragma unroll
+        for (int a = 0; a < AHEAD; ++a) load_sb((uint32_t)wg + 2u * a, sbq[a]);
         for (uint32_t it = (uint32_t)wg; it < total; it += 2) {
-            uint32_t sb_next[4];
-            load_sb(it + 2, sb_next);
+            uint32_t sb[4], sb_next[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sb[i] = sbq[0][i];
+            load_sb(it + 2u * AHEAD, sb_next);
             const int lt = (int)(it / (uint32_t)KT), kt = (int)(it - (uint32_t)lt * KT);
             const int s = it % STAGES, j = it % AST;
-            if (!mbar_wait(&wfull[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort) ||
-                !mbar_wait(&aempty[j], ((it / AST) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY, peer_abort))
+            if (!TR_WAIT(warp == 8 ? 5 : 15, mbar_wait<CG == 2>(&wfull[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort)) ||
+                !TR_WAIT(warp == 8 ? 6 : 15, mbar_wait<CG == 2>(&aempty[j], ((it / AST) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY, peer_abort)))
                 break;
             uint32_t r[32];
+#ifdef QL_EXP_NODQ
+            if (kt < p.ktw) {
+                const uint32_t *wr = reinterpret_cast<const uint32_t *>(smem + C::SMEM_W + s * C::W_STAGE_BYTES + row * C::W_ROW_BYTES);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) r[i] = wr[i % (C::W_ROW_BYTES / 4)] ^ sb[i & 3];
+            } else
+#endif
             if (kt < p.ktw) {
                 const uint32_t s0 = sb[0] * 0x10001u, b0 = sb[1] * 0x10001u;  // bf16x2 broadcast
                 const uint32_t s1 = sb[2] * 0x10001u, b1 = sb[3] * 0x10001u;
@@ -436,14 +475,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive_cluster(leader(&afull[j]));
+                if (CG == 2 && rank != 0) mbar_arrive_cluster(leader(&afull[j]));
+                else mbar_arrive(&afull[j]);
                 mbar_arrive(&empty[s]);
             }
 #pragma unroll
-            for (int i = 0; i < 4; ++i) sb[i] = sb_next[i];
+            for (int a = 0; a + 1 < AHEAD; ++a)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sbq[a][i] = sbq[a + 1][i];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sbq[AHEAD - 1][i] = sb_next[i];
         }
     }
 
+#ifdef QL_TRACE
+    if (threadIdx.x == 32) g_trace[7][blockIdx.x % 160] += clock64();  // kernel span of warp 1
+#endif
     tc_fence_before();
     // no CTA of a pair may exit while its peer can still signal its barriers
     if (CG == 2) cluster_sync_all();
@@ -525,6 +572,7 @@ static int launch_t(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensor
         int mc = 0;
         if (CG == 1 || cudaOccupancyMaxActiveClusters(&mc, kfn, &cfg) != cudaSuccess || mc <= 0) mc = sms / CG;
         max_clusters = mc;
+        if (getenv("QL_DEBUG")) fprintf(stderr, "qgemm CG=%d: %d resident clusters, smem %d\n", CG, mc, C::SMEM_TOTAL);
     }
     const int clusters = tiles < max_clusters ? tiles : max_clusters;
     cfg.gridDim = dim3((unsigned)(clusters * CG));
@@ -533,6 +581,12 @@ static int launch_t(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensor
 }
 
 }  // namespace gemm
+
+#ifdef QL_TRACE
+extern "C" int ql_debug_trace(unsigned long long *out, int) {
+    return (int)cudaMemcpyFromSymbol(out, gemm::g_trace, sizeof(gemm::g_trace));
+}
+#endif
 
 // x [M,K] bf16, W packed [N,K] (+ W3 for SwiGLU), scales/biases bf16.
 // lora_t: [M, r_pad] bf16 (r_pad = round_up(rank, 64)) already holding s.(x.A), or null.

@@ -140,15 +140,25 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  : "memory");
 }
 
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
+    if (CLUSTER)  // arrivals may come from the paired CTA: acquire at cluster scope
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
     return ok != 0;
 }
 
@@ -166,12 +176,13 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
                                           unsigned code, uint32_t peer_abort = 0) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait<CLUSTER>(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait<CLUSTER>(bar, parity)) return true;
         if ((i & 63u) == 0) {
             if (*abort) return false;
             if (globaltimer_ns() - t0 > kWaitLimitNs) {

@@ -5,7 +5,7 @@ dequantize / quantized_matmul``; ``AdaptableLinear``, ``Adapter``, ``TokenEmbedd
 ``quant::{lin, embedding, quantize_map, DEFAULT_GROUP_SIZE}``) on top of the C ABI in
 include/qlinear.h.  All arithmetic runs in libqlinear.so (CUDA, sm_100a).
 """
-from ._lib import (ACT_GELU_ERF, ACT_GELU_TANH, ACT_NONE, ACT_SWIGLU, KERNEL_AUTO, KERNEL_GEMM, KERNEL_GEMM_1SM,
+from ._lib import (ACT_GELU_ERF, ACT_GELU_TANH, ACT_NONE, ACT_SWIGLU, KERNEL_AUTO, KERNEL_GEMM, KERNEL_GEMM_PAIR,
                    KERNEL_GEMV, KERNEL_GENERIC, QlError, device_error)
 from .nn import (DEFAULT_GROUP_SIZE, AdaptableLinear, Linear, Lokr, Lora, QuantizedLinear,
                  TokenEmbedding)
@@ -13,7 +13,7 @@ from .ops import dequantize, dequantize_rows, quantize, quantized_matmul, worksp
 from .quant import embedding, lin, packed_bits, quantize_map
 
 __all__ = [
-    "ACT_GELU_ERF", "ACT_GELU_TANH", "ACT_NONE", "ACT_SWIGLU", "KERNEL_AUTO", "KERNEL_GEMM", "KERNEL_GEMM_1SM",
+    "ACT_GELU_ERF", "ACT_GELU_TANH", "ACT_NONE", "ACT_SWIGLU", "KERNEL_AUTO", "KERNEL_GEMM", "KERNEL_GEMM_PAIR",
     "KERNEL_GEMV", "KERNEL_GENERIC", "QlError", "device_error", "DEFAULT_GROUP_SIZE",
     "AdaptableLinear", "Linear", "Lokr", "Lora", "QuantizedLinear", "TokenEmbedding", "dequantize",
     "dequantize_rows", "quantize", "quantized_matmul", "workspace_size", "embedding", "lin",

@@ -1,7 +1,7 @@
 """One quantized_matmul shape, timed with CUDA events (also the small case used for ncu
 captures).  Usage:
 
-    python -m qlinear.bench_case M N K BITS [ACT|none] [REPS] [gemm|gemv|auto]
+    python -m qlinear.bench_case M N K BITS [ACT|none] [REPS] [gemm|gemm2|gemv|auto]
 
 (run with mlx-gen_b200 on PYTHONPATH).  Prints time per call and TFLOP/s / GB/s.
 Weights ~N(0, 0.02) bf16 quantized on the device (group 64), x ~N(0, 1), bias ~N(0, 0.02).
@@ -17,7 +17,7 @@ def main(argv):
     M, N, K, bits = (int(v) for v in argv[:4])
     act = argv[4] if len(argv) > 4 and argv[4] != "none" else None
     reps = int(argv[5]) if len(argv) > 5 else 20
-    kernel = {"gemm": qlinear.KERNEL_GEMM, "gemv": qlinear.KERNEL_GEMV, "auto": qlinear.KERNEL_AUTO}[
+    kernel = {"gemm": qlinear.KERNEL_GEMM, "gemm2": qlinear.KERNEL_GEMM_PAIR, "gemv": qlinear.KERNEL_GEMV, "auto": qlinear.KERNEL_AUTO}[
         argv[6] if len(argv) > 6 else "auto"]
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev).manual_seed(0)

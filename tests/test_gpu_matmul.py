@@ -12,7 +12,7 @@ from helpers import assert_bf16_close, np2t, rand_bf16, t2np
 
 pytestmark = pytest.mark.gpu
 GEMV, GEMM, GENERIC = qlinear.KERNEL_GEMV, qlinear.KERNEL_GEMM, qlinear.KERNEL_GENERIC
-GEMM1 = qlinear.KERNEL_GEMM_1SM
+GEMM2 = qlinear.KERNEL_GEMM_PAIR
 
 
 def make_case(dev, M, N, K, gs, bits, seed, wstd=0.02):
@@ -43,7 +43,7 @@ def test_gemv_parity(dev, bits, gs, M):
     assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(O.quantized_matmul(x, wq, s, b, gs, bits)), what="gemv")
 
 
-@pytest.mark.parametrize("kernel", [GEMM, GEMM1])
+@pytest.mark.parametrize("kernel", [GEMM, GEMM2])
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("gs", [32, 64, 128])
 @pytest.mark.parametrize("M,N,K", [(9, 128, 64), (256, 128, 256), (300, 200, 448), (513, 384, 128)])
@@ -57,7 +57,7 @@ def test_gemm_parity(dev, bits, gs, M, N, K, kernel):
     assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(O.quantized_matmul(x, wq, s, b, gs, bits)), what="gemm")
 
 
-@pytest.mark.parametrize("kernel", [GEMV, GEMM, GEMM1, GENERIC])
+@pytest.mark.parametrize("kernel", [GEMV, GEMM, GEMM2, GENERIC])
 @pytest.mark.parametrize("act", [None, "gelu_tanh", "gelu"])
 def test_bias_act_epilogue(dev, kernel, act):
     M = 4 if kernel == GEMV else 260
@@ -70,7 +70,7 @@ def test_bias_act_epilogue(dev, kernel, act):
     assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), ulps=4 if act else 2, what=f"bias+{act}")
 
 
-@pytest.mark.parametrize("kernel", [GEMV, GEMM, GEMM1, GENERIC])
+@pytest.mark.parametrize("kernel", [GEMV, GEMM, GEMM2, GENERIC])
 @pytest.mark.parametrize("bits", [4, 8])
 def test_swiglu_epilogue(dev, kernel, bits):
     M = 5 if kernel == GEMV else 300
@@ -85,7 +85,7 @@ def test_swiglu_epilogue(dev, kernel, bits):
     assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(O.swiglu(h1, h3)), ulps=4, what="swiglu")
 
 
-@pytest.mark.parametrize("kernel", [GEMV, GEMM, GEMM1, GENERIC])
+@pytest.mark.parametrize("kernel", [GEMV, GEMM, GEMM2, GENERIC])
 @pytest.mark.parametrize("rank", [8, 32, 96])
 def test_lora_epilogue(dev, kernel, rank):
     """LoRA residual scale*(x.A).B fused into the accumulator (src/adapters.rs:260-270).  The
