@@ -6,6 +6,7 @@
 #include "api.cu"
 #include "qgemm_sm100.cu"
 #include "qgemv.cu"
+#include "qgemv_tma.cu"
 #include "qmm_generic.cu"
 #include "quantize.cu"
 #include "noalloc.cu"

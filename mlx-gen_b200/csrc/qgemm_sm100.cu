@@ -563,7 +563,7 @@ static int launch_t(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensor
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = CG == 2 ? 1 : 0;  // a plain launch for the 1-CTA kernel
     // persistent grid: as many clusters as can be resident at once (pairs need two free
     // SMs of one GPC), never more than there are tiles
     static int max_clusters = 0;

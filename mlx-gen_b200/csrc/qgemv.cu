@@ -19,6 +19,8 @@
 // Dequantized weights are exact bf16 roundings of fma(code, scale, bias) --
 // the same values ql_dequantize produces -- so GEMV, GEMM and dequant+matmul
 // agree on the operand.
+#include <stdlib.h>
+
 #include "ql_common.cuh"
 
 namespace ql {
@@ -271,10 +273,21 @@ __global__ void __launch_bounds__(WARPS * 32, 2) qgemv_kernel(const Params p) {
 
 }  // namespace gemv
 
+bool qgemv_tma_supported(int64_t M, int64_t K, int gs);
+int launch_qgemv_tma(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales,
+                     const void *biases, const uint32_t *wq2, const void *scales2, const void *biases2,
+                     int64_t N, int gs, int bits, const void *bias, const void *bias2, int act,
+                     const void *lora_t, const void *lora_b, int64_t rank, void *y, cudaStream_t st);
+
 int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales,
                  const void *biases, const uint32_t *wq2, const void *scales2, const void *biases2,
                  int64_t N, int gs, int bits, const void *bias, const void *bias2, int act,
                  const void *lora_t, const void *lora_b, int64_t rank, void *y, cudaStream_t st) {
+    // the TMA-fed kernel (qgemv_tma.cu) whenever the shape allows it
+    static const bool force_regs = getenv("QL_GEMV_REGS") != nullptr;  // profiling switch
+    if (!force_regs && qgemv_tma_supported(M, K, gs))
+        return launch_qgemv_tma(x, M, K, wq, scales, biases, wq2, scales2, biases2, N, gs, bits, bias, bias2, act,
+                                lora_t, lora_b, rank, y, st);
     using namespace gemv;
     Params p{};
     p.x = (const __nv_bfloat16 *)x;

@@ -1,0 +1,400 @@
+// qgemv_tma.cu -- small-M (M <= 8) quantized matmul, TMA-fed (the default GEMV).
+//
+// y[M, N] = x[M, K] . dequant(W)[N, K]^T, bf16 activations and scales.  The path the
+// reference takes for decode-time and timestep linears (quantized_matmul with few rows,
+// src/adapters.rs:309-317) is HBM-bound, so this kernel is built to keep HBM busy
+// with as few instructions per weight byte as possible:
+//
+//   * A producer warp streams each 16-row strip of packed W (plus its scales and
+//     biases) through a ring of shared-memory stages with TMA, 1024 codes of K per
+//     stage.  The W tensor map is 3-D -- (words of a 32-code run, row, run) -- so a
+//     stage lands as [run][row][run words]: the eight consumer warps then read it
+//     without bank conflicts.  Weights do not depend on the previous kernel, so the
+//     producer starts before griddepcontrol.wait (programmatic dependent launch) and
+//     the stream of one launch overlaps the tail of the previous one.
+//   * Consumers never apply scale and bias per element.  Codes become exact bf16
+//     values 128 + q with one shift and one lop3 per pair, feed mma.sync m16n8k16
+//     (tokens padded to 8) and accumulate per group; each finished group is folded
+//     in as  y += s * D + (b - 128 s) * sum_k x_k  with the per-group sums of x
+//     precomputed once per CTA.  Q8 codes are split into nibbles (q = 16 h + l)
+//     accumulated separately.  Mathematically this is sum_k x_k (q_k s + b): the
+//     weights are used exactly, without the bf16 rounding of the dequantized value.
+//   * The 8 warps split each stage's K (128 codes each); per-strip partial tiles are
+//     summed through shared memory and the fused epilogue (bias, LoRA, GELU, SwiGLU)
+//     writes y.
+// Used when K is a multiple of 8 groups (TMA row pitch of the scales); other shapes use
+// the register-fed kernel in qgemv.cu.
+#include "ql_common.cuh"
+
+namespace ql {
+namespace gemv2 {
+
+constexpr int CWARPS = 8;            // consumer warps
+constexpr int NTHREADS = (CWARPS + 1) * 32;
+constexpr int KS = 1024;             // codes of K per stage
+constexpr int RUNS = KS / 32;        // 32-code runs per stage
+
+struct Params {
+    int M, N, K, gs, G, nks;         // nks: stages per strip
+    int act;
+    const __nv_bfloat16 *x;
+    const __nv_bfloat16 *bias, *bias2;
+    const __nv_bfloat16 *lora_t, *lora_b;
+    int rank, rpad;
+    __nv_bfloat16 *y;
+};
+
+template <int BITS, bool SWIGLU>
+struct Cfg {
+    static constexpr int NPASS = SWIGLU ? 2 : 1;
+    static constexpr int RUNW = BITS;                       // words per 32-code run
+    static constexpr int W_BYTES = 16 * KS * BITS / 8;      // one pass, one stage
+    static constexpr int STAGES = BITS == 4 ? (SWIGLU ? 4 : 6) : (SWIGLU ? 3 : 4);
+};
+
+__device__ __forceinline__ void mma16816(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// bf16x2 (128 + code_lo, 128 + code_hi) from the nibbles at bit 4j and 16 + 4j
+__device__ __forceinline__ uint32_t nib2(uint32_t w, int j) {
+    return ((w >> (4 * j)) & 0x000f000fu) | 0x43004300u;
+}
+
+template <int BITS, bool SWIGLU, int GS>
+__global__ void __launch_bounds__(NTHREADS, 2)
+    qgemv_tma_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
+                     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_w2,
+                     const __grid_constant__ CUtensorMap tm_s2, const __grid_constant__ CUtensorMap tm_b2,
+                     const Params p) {
+    using C = Cfg<BITS, SWIGLU>;
+    constexpr int NPASS = C::NPASS, STAGES = C::STAGES;
+    constexpr int GPS = KS / GS;                            // groups per stage
+    constexpr int SB_BYTES = 16 * GPS * 2;                  // scales (or biases) per stage
+    constexpr int STAGE_BYTES = NPASS * (C::W_BYTES + 2 * SB_BYTES);
+    const int nstrips = (p.N + 15) / 16;
+    const int nruns = p.nks * RUNS;                          // runs of x staged (zero past K)
+    const int xstride = nruns * 64 + ((nruns & 1) ? 0 : 64);  // bytes per token in smem
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *stages = smem;                                           // STAGES * STAGE_BYTES
+    uint8_t *xs = stages + STAGES * STAGE_BYTES;                      // M * xstride
+    float *xsum = reinterpret_cast<float *>(xs + p.M * xstride);      // [8][G]
+    float *red = xsum + 8 * p.G;                                      // [NPASS][8][16][8]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(red + NPASS * CWARPS * 128);
+    uint64_t *full = bars, *empty = bars + STAGES;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 2 * STAGES);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], CWARPS);
+        }
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    if (warp == CWARPS) {
+        // ---------------------------------------------------------------- TMA producer
+        // Weights, scales and biases do not depend on the previous kernel: stream them
+        // before griddepcontrol.wait.
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int st = blockIdx.x; st < nstrips && !*abort_flag; st += gridDim.x) {
+                for (int kc = 0; kc < p.nks; ++kc, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY)) break;
+                    uint8_t *sp = stages + s * STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+#pragma unroll
+                    for (int ps = 0; ps < NPASS; ++ps) {
+                        uint8_t *pp = sp + ps * (C::W_BYTES + 2 * SB_BYTES);
+                        tma_load_3d(pp, ps ? &tm_w2 : &tm_w, &full[s], 0, st * 16, kc * RUNS);
+                        tma_load_2d(pp + C::W_BYTES, ps ? &tm_s2 : &tm_s, &full[s], kc * GPS, st * 16);
+                        tma_load_2d(pp + C::W_BYTES + SB_BYTES, ps ? &tm_b2 : &tm_b, &full[s], kc * GPS, st * 16);
+                    }
+                }
+            }
+        }
+        return;  // the producer takes no part in the consumers' named barriers
+    }
+
+    // -------------------------------------------------------------------- consumers
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int tid = threadIdx.x;  // 0 .. 255
+    // x -> smem, permuted so that lane c of a warp reads its four bf16 pairs of a run in
+    // one 16-byte load: Q4 pairs (0,4) (1,5) (2,6) (3,7), Q8 pairs (0,2) (1,3) (4,6) (5,7)
+    // of the lane's 8 consecutive codes.
+    for (int u = tid; u < p.M * nruns * 4; u += CWARPS * 32) {
+        const int m = u / (nruns * 4), rc = u - m * nruns * 4;   // rc = run * 4 + c
+        const int k = rc * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (k < p.K) v = __ldg(reinterpret_cast<const uint4 *>(p.x + (int64_t)m * p.K + k));
+        uint4 o;
+        if (BITS == 4) {
+            o.x = prmt(v.x, v.z, 0x5410u);  // (0,4)
+            o.y = prmt(v.x, v.z, 0x7632u);  // (1,5)
+            o.z = prmt(v.y, v.w, 0x5410u);  // (2,6)
+            o.w = prmt(v.y, v.w, 0x7632u);  // (3,7)
+        } else {
+            o.x = prmt(v.x, v.y, 0x5410u);  // (0,2)
+            o.y = prmt(v.x, v.y, 0x7632u);  // (1,3)
+            o.z = prmt(v.z, v.w, 0x5410u);  // (4,6)
+            o.w = prmt(v.z, v.w, 0x7632u);  // (5,7)
+        }
+        *reinterpret_cast<uint4 *>(xs + m * xstride + rc * 16) = o;
+    }
+    named_bar_sync(1, CWARPS * 32);
+    // per-group sums of x (fp32) from the staged copy (any order of the group's values),
+    // zero for padded tokens
+    for (int u = tid; u < 8 * p.G; u += CWARPS * 32) {
+        const int m = u / p.G, gi = u - m * p.G;
+        float acc = 0.f;
+        if (m < p.M) {
+            const uint4 *xp = reinterpret_cast<const uint4 *>(xs + m * xstride) + gi * (GS / 8);
+#pragma unroll 4
+            for (int e = 0; e < GS / 8; ++e) {
+                const uint4 v = xp[e];
+                acc += (bf16lo(v.x) + bf16hi(v.x)) + (bf16lo(v.y) + bf16hi(v.y)) + (bf16lo(v.z) + bf16hi(v.z)) +
+                       (bf16lo(v.w) + bf16hi(v.w));
+            }
+        }
+        xsum[u] = acc;
+    }
+    named_bar_sync(1, CWARPS * 32);
+
+    const int g = lane >> 2, c = lane & 3;
+    const float cfold = BITS == 4 ? 128.f : 2176.f;  // offset folded back per group
+    constexpr int runs_per_group = GS / 32;
+    uint32_t it = 0;
+    for (int st = blockIdx.x; st < nstrips; st += gridDim.x) {
+        float acc[NPASS][4] = {};
+        bool ok = true;
+        for (int kc = 0; kc < p.nks; ++kc, ++it) {
+            const int s = it % STAGES;
+            if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL)) {
+                ok = false;
+                break;
+            }
+            const uint8_t *sp = stages + s * STAGE_BYTES;
+#pragma unroll
+            for (int ps = 0; ps < NPASS; ++ps) {
+                const uint8_t *wp = sp + ps * (C::W_BYTES + 2 * SB_BYTES);
+                const uint16_t *sc = reinterpret_cast<const uint16_t *>(wp + C::W_BYTES);
+                const uint16_t *bi = reinterpret_cast<const uint16_t *>(wp + C::W_BYTES + SB_BYTES);
+                // two accumulators per nibble plane break the MMA dependency chain
+                float d[4] = {0.f, 0.f, 0.f, 0.f}, dh[4] = {0.f, 0.f, 0.f, 0.f};
+                float e[4] = {0.f, 0.f, 0.f, 0.f}, eh[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int rr = 0; rr < 4; ++rr) {
+                    const int r = warp * 4 + rr;          // run within the stage
+                    uint4 X = make_uint4(0, 0, 0, 0);  // tokens past M are zero
+                    if (g < p.M) X = *reinterpret_cast<const uint4 *>(xs + g * xstride + ((kc * RUNS + r) * 4 + c) * 16);
+                    if constexpr (BITS == 4) {
+                        const uint32_t wg = *reinterpret_cast<const uint32_t *>(wp + ((r * 16 + g) * 4 + c) * 4);
+                        const uint32_t wh = *reinterpret_cast<const uint32_t *>(wp + ((r * 16 + g + 8) * 4 + c) * 4);
+                        mma16816(d, nib2(wg, 0), nib2(wh, 0), nib2(wg, 1), nib2(wh, 1), X.x, X.y);
+                        mma16816(e, nib2(wg, 2), nib2(wh, 2), nib2(wg, 3), nib2(wh, 3), X.z, X.w);
+                    } else {
+                        const uint2 wg = *reinterpret_cast<const uint2 *>(wp + ((r * 16 + g) * 8 + 2 * c) * 4);
+                        const uint2 wh = *reinterpret_cast<const uint2 *>(wp + ((r * 16 + g + 8) * 8 + 2 * c) * 4);
+                        // low nibbles: (l0,l2) at shift 0, (l1,l3) at shift 8; high: 4, 12
+                        mma16816(d, nib2(wg.x, 0), nib2(wh.x, 0), nib2(wg.x, 2), nib2(wh.x, 2), X.x, X.y);
+                        mma16816(e, nib2(wg.y, 0), nib2(wh.y, 0), nib2(wg.y, 2), nib2(wh.y, 2), X.z, X.w);
+                        mma16816(dh, nib2(wg.x, 1), nib2(wh.x, 1), nib2(wg.x, 3), nib2(wh.x, 3), X.x, X.y);
+                        mma16816(eh, nib2(wg.y, 1), nib2(wh.y, 1), nib2(wg.y, 3), nib2(wh.y, 3), X.z, X.w);
+                    }
+                    if ((r + 1) % runs_per_group == 0) {
+                        // fold the finished group: y += s D + (b - cfold s) X
+                        const int gl = (r * 32) / GS;                   // group within the stage
+                        const int gg = kc * GPS + gl;                   // global group
+                        const float sg = bf16lo((uint32_t)sc[g * GPS + gl]);
+                        const float sh = bf16lo((uint32_t)sc[(g + 8) * GPS + gl]);
+                        const float bg = bf16lo((uint32_t)bi[g * GPS + gl]) - cfold * sg;
+                        const float bh = bf16lo((uint32_t)bi[(g + 8) * GPS + gl]) - cfold * sh;
+                        const float x0 = gg < p.G ? xsum[(2 * c) * p.G + gg] : 0.f;
+                        const float x1 = gg < p.G ? xsum[(2 * c + 1) * p.G + gg] : 0.f;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            d[i] += e[i];
+                            e[i] = 0.f;
+                            if (BITS == 8) {
+                                d[i] = fmaf(16.f, dh[i] + eh[i], d[i]);
+                                dh[i] = 0.f;
+                                eh[i] = 0.f;
+                            }
+                        }
+                        acc[ps][0] += fmaf(sg, d[0], bg * x0);
+                        acc[ps][1] += fmaf(sg, d[1], bg * x1);
+                        acc[ps][2] += fmaf(sh, d[2], bh * x0);
+                        acc[ps][3] += fmaf(sh, d[3], bh * x1);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) d[i] = 0.f;
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if (!ok) break;
+        // partial tiles of the 8 warps -> one 16 x 8 tile -> epilogue
+#pragma unroll
+        for (int ps = 0; ps < NPASS; ++ps) {
+            float *rp = red + (ps * CWARPS + warp) * 128;
+            rp[g * 8 + 2 * c] = acc[ps][0];
+            rp[g * 8 + 2 * c + 1] = acc[ps][1];
+            rp[(g + 8) * 8 + 2 * c] = acc[ps][2];
+            rp[(g + 8) * 8 + 2 * c + 1] = acc[ps][3];
+        }
+        named_bar_sync(1, CWARPS * 32);
+        if (tid < 128) {
+            const int r = tid >> 3, m = tid & 7, n = st * 16 + r;
+            if (n < p.N && m < p.M) {
+                float a = 0.f, a2 = 0.f;
+#pragma unroll
+                for (int w = 0; w < CWARPS; ++w) {
+                    a += red[w * 128 + r * 8 + m];
+                    if (SWIGLU) a2 += red[(CWARPS + w) * 128 + r * 8 + m];
+                }
+                if (p.lora_t) {
+                    const __nv_bfloat16 *t = p.lora_t + (int64_t)m * p.rpad;
+                    for (int j = 0; j < p.rank; ++j)
+                        a += __bfloat162float(t[j]) * __bfloat162float(p.lora_b[(int64_t)j * p.N + n]);
+                }
+                float v = round_bf16(a);
+                if (p.bias) v = round_bf16(v + __bfloat162float(p.bias[n]));
+                if (SWIGLU) {
+                    float uu = round_bf16(a2);
+                    if (p.bias2) uu = round_bf16(uu + __bfloat162float(p.bias2[n]));
+                    v = v / (1.0f + __expf(-v)) * uu;
+                } else if (p.act == QL_ACT_GELU_TANH) {
+                    float t;
+                    const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+                    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(inner));
+                    v = 0.5f * v * (1.0f + t);
+                } else if (p.act == QL_ACT_GELU_ERF) {
+                    v = 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
+                }
+                p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(v);
+            }
+        }
+        named_bar_sync(1, CWARPS * 32);
+    }
+}
+
+static int make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, int rank, const uint64_t *dims,
+                    const uint64_t *strides_bytes, const uint32_t *box) {
+    gemm::PFN_encodeTiled enc = gemm::get_encode();
+    if (!enc) return fail(QL_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t d[3], st[2];
+    cuuint32_t b[3], e[3] = {1, 1, 1};
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        b[i] = box[i];
+    }
+    for (int i = 0; i + 1 < rank; ++i) st[i] = strides_bytes[i];
+    CUresult r = enc(map, dt, (cuuint32_t)rank, const_cast<void *>(base), d, st, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(QL_ECUDA, "cuTensorMapEncodeTiled (gemv) failed (%d)", (int)r);
+    return QL_OK;
+}
+
+template <int BITS, bool SWIGLU, int GS>
+static int launch_t(const CUtensorMap *maps, const Params &p, cudaStream_t st) {
+    using C = Cfg<BITS, SWIGLU>;
+    auto kfn = qgemv_tma_kernel<BITS, SWIGLU, GS>;
+    const int GPS = KS / p.gs;
+    const size_t stage_bytes = (size_t)C::NPASS * (C::W_BYTES + 2 * 16 * GPS * 2);
+    const int nruns = p.nks * RUNS;
+    const size_t xstride = (size_t)nruns * 64 + ((nruns & 1) ? 0 : 64);
+    const size_t smem = 1024 + C::STAGES * stage_bytes + (size_t)p.M * xstride + 8 * (size_t)p.G * 4 +
+                        (size_t)C::NPASS * CWARPS * 128 * 4 + 2 * C::STAGES * 8 + 16;
+    if (smem > 227 * 1024) return fail(QL_EUNSUPPORTED, "GEMV: K too large for the staged kernel");
+    QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int dev = 0, sms = 148;
+    QL_CUDA_TRY(cudaGetDevice(&dev));
+    QL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int nstrips = (p.N + 15) / 16;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(nstrips < 2 * sms ? nstrips : 2 * sms));
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    QL_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p));
+    return QL_OK;
+}
+
+}  // namespace gemv2
+
+// True when the staged kernel handles this shape (scales' row pitch must be a multiple of
+// 16 bytes for TMA, i.e. K a multiple of 8 groups).
+bool qgemv_tma_supported(int64_t M, int64_t K, int gs) { return M >= 1 && M <= 8 && (K / gs) % 8 == 0; }
+
+int launch_qgemv_tma(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales,
+                     const void *biases, const uint32_t *wq2, const void *scales2, const void *biases2,
+                     int64_t N, int gs, int bits, const void *bias, const void *bias2, int act,
+                     const void *lora_t, const void *lora_b, int64_t rank, void *y, cudaStream_t st) {
+    using namespace gemv2;
+    const bool sw = act == QL_ACT_SWIGLU;
+    Params p{};
+    p.M = (int)M;
+    p.N = (int)N;
+    p.K = (int)K;
+    p.gs = gs;
+    p.G = (int)(K / gs);
+    p.nks = (int)((K + KS - 1) / KS);
+    p.act = act;
+    p.x = (const __nv_bfloat16 *)x;
+    p.bias = (const __nv_bfloat16 *)bias;
+    p.bias2 = (const __nv_bfloat16 *)bias2;
+    p.lora_t = (const __nv_bfloat16 *)lora_t;
+    p.lora_b = (const __nv_bfloat16 *)lora_b;
+    p.rank = (int)rank;
+    p.rpad = (int)(rank > 0 ? (rank + 63) / 64 * 64 : 0);
+    p.y = (__nv_bfloat16 *)y;
+
+    CUtensorMap maps[6];
+    const uint64_t runw = (uint64_t)bits;  // words per 32-code run
+    for (int ps = 0; ps < (sw ? 2 : 1); ++ps) {
+        const uint32_t *w = ps ? wq2 : wq;
+        const void *s = ps ? scales2 : scales, *b = ps ? biases2 : biases;
+        // W as (run words, row, run): strides row = K*bits/8 bytes, run = runw*4 bytes
+        const uint64_t wd[3] = {runw, (uint64_t)N, (uint64_t)(K / 32)};
+        const uint64_t ws[2] = {(uint64_t)K * bits / 8, runw * 4};
+        const uint32_t wb[3] = {(uint32_t)runw, 16, (uint32_t)RUNS};
+        if (int rc = make_map(&maps[3 * ps], CU_TENSOR_MAP_DATA_TYPE_UINT32, w, 3, wd, ws, wb)) return rc;
+        const uint64_t sd[2] = {(uint64_t)p.G, (uint64_t)N};
+        const uint64_t ss[1] = {(uint64_t)p.G * 2};
+        const uint32_t sbx[2] = {(uint32_t)(KS / gs), 16};
+        if (int rc = make_map(&maps[3 * ps + 1], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, s, 2, sd, ss, sbx)) return rc;
+        if (int rc = make_map(&maps[3 * ps + 2], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, 2, sd, ss, sbx)) return rc;
+    }
+    if (!sw)
+        for (int i = 0; i < 3; ++i) maps[3 + i] = maps[i];
+#define QL_GEMV_GS(GS_)                                                                          \
+    if (gs == GS_) {                                                                             \
+        if (bits == 4) return sw ? launch_t<4, true, GS_>(maps, p, st) : launch_t<4, false, GS_>(maps, p, st); \
+        return sw ? launch_t<8, true, GS_>(maps, p, st) : launch_t<8, false, GS_>(maps, p, st);   \
+    }
+    QL_GEMV_GS(32)
+    QL_GEMV_GS(64)
+    QL_GEMV_GS(128)
+#undef QL_GEMV_GS
+    return fail(QL_EUNSUPPORTED, "group size %d", gs);
+}
+
+}  // namespace ql

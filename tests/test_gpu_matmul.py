@@ -36,8 +36,11 @@ def test_fixture_qmm_f32(golden, dev, bits):
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("gs", [32, 64, 128])
 @pytest.mark.parametrize("M", [1, 2, 3, 8])
-def test_gemv_parity(dev, bits, gs, M):
-    N, K = 200, 384
+@pytest.mark.parametrize("K", [384, 1024, 2560])
+def test_gemv_parity(dev, bits, gs, M, K):
+    """K=384 runs the register-fed GEMV; K=1024 / 2560 (K a multiple of 8 groups) the
+    TMA-fed one, 2560 with a partial last stage."""
+    N = 200
     _, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 100 * M + gs + bits)
     y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, kernel=GEMV)
     assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(O.quantized_matmul(x, wq, s, b, gs, bits)), what="gemv")
@@ -138,3 +141,37 @@ def test_full_size_gemm_properties(dev, bits, N, K, act):
         err = (y.float() - ref_all).abs()
         assert err.max() <= ref_all.abs().max() * 2 ** -6
         assert (err.norm() / ref_all.norm()) <= 4e-3
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("epi", ["bias_gelu", "swiglu", "lora"])
+def test_gemv_tma_epilogues(dev, bits, epi):
+    """Fused epilogues on the TMA-fed GEMV (K a multiple of 8 groups).  This kernel uses the
+    weights exactly (no bf16 rounding of the dequantized value) while the oracle, like MLX,
+    rounds them to bf16 first; with GELU / SwiGLU (rounded op by op in the reference)
+    relative L2 is allowed 6e-3."""
+    M, N, K, gs = 5, 176, 2048, 64
+    rng, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 17)
+    bias = rand_bf16((N,), 0.2, rng)
+    if epi == "bias_gelu":
+        y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, bias=np2t(bias, dev), act="gelu_tanh",
+                                     kernel=GEMV)
+        ref = O.quantized_matmul(x, wq, s, b, gs, bits, bias=bias, act=O.ACT_GELU_TANH)
+        tol = dict(ulps=4, rl2=6e-3)
+    elif epi == "swiglu":
+        w3 = rand_bf16((N, K), 0.02, rng)
+        wq3, s3, b3 = O.quantize(w3, gs, bits)
+        y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, act="swiglu",
+                                     up=(np2t(wq3, dev), np2t(s3, dev), np2t(b3, dev)), kernel=GEMV)
+        ref = O.swiglu(O.quantized_matmul(x, wq, s, b, gs, bits), O.quantized_matmul(x, wq3, s3, b3, gs, bits))
+        tol = dict(ulps=4, rl2=6e-3)
+    else:
+        A = rand_bf16((K, 32), 1.0 / np.sqrt(32), rng)
+        B = rand_bf16((32, N), 0.01, rng)
+        y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, bias=np2t(bias, dev),
+                                     lora=(np2t(A, dev), np2t(B, dev), 0.5), kernel=GEMV)
+        ref = O.quantized_matmul(x, wq, s, b, gs, bits, bias=bias, lora_a=A, lora_b=B, lora_scale=0.5)
+        tol = dict(ulps=4, atol_frac=2 ** -7)
+    torch.cuda.synchronize()
+    assert qlinear.device_error() == 0
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), what=f"gemv-tma {epi}", **tol)
