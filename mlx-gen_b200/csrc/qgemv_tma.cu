@@ -7,9 +7,8 @@
 //
 //   * A producer warp streams each 16-row strip of packed W (plus its scales and
 //     biases) through a ring of shared-memory stages with TMA, 1024 codes of K per
-//     stage.  The W tensor map is 3-D -- (words of a 32-code run, row, run) -- so a
-//     stage lands as [run][row][run words]: the eight consumer warps then read it
-//     without bank conflicts.  Weights do not depend on the previous kernel, so the
+//     stage, in boxes of 16 rows x 128 bytes with the 128-byte swizzle so that the
+//     eight rows a consumer instruction touches land in different banks.  Weights do not depend on the previous kernel, so the
 //     producer starts before griddepcontrol.wait (programmatic dependent launch) and
 //     the stream of one launch overlaps the tail of the previous one.
 //   * Consumers never apply scale and bias per element.  Codes become exact bf16
@@ -19,9 +18,9 @@
 //     precomputed once per CTA.  Q8 codes are split into nibbles (q = 16 h + l)
 //     accumulated separately.  Mathematically this is sum_k x_k (q_k s + b): the
 //     weights are used exactly, without the bf16 rounding of the dequantized value.
-//   * The 8 warps split each stage's K (128 codes each); per-strip partial tiles are
-//     summed through shared memory and the fused epilogue (bias, LoRA, GELU, SwiGLU)
-//     writes y.
+//   * The 8 consumer warps split each stage's K (128 codes each); per-strip partial
+//     tiles are summed through shared memory and the fused epilogue (bias, LoRA, GELU,
+//     SwiGLU) writes y.
 // Used when K is a multiple of 8 groups (TMA row pitch of the scales); other shapes use
 // the register-fed kernel in qgemv.cu.
 #include "ql_common.cuh"
@@ -76,7 +75,9 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     constexpr int NPASS = C::NPASS, STAGES = C::STAGES;
     constexpr int GPS = KS / GS;                            // groups per stage
     constexpr int SB_BYTES = 16 * GPS * 2;                  // scales (or biases) per stage
-    constexpr int STAGE_BYTES = NPASS * (C::W_BYTES + 2 * SB_BYTES);
+    constexpr int PASS_BYTES = (C::W_BYTES + 2 * SB_BYTES + 1023) / 1024 * 1024;  // swizzled boxes: 1 KB aligned
+    constexpr int STAGE_BYTES = NPASS * PASS_BYTES;
+    constexpr int WBOXES = KS * BITS / 8 / 128;             // 128-byte-wide boxes per stage
     const int nstrips = (p.N + 15) / 16;
     const int nruns = p.nks * RUNS;                          // runs of x staged (zero past K)
     const int xstride = nruns * 64 + ((nruns & 1) ? 0 : 64);  // bytes per token in smem
@@ -86,8 +87,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     uint8_t *stages = smem;                                           // STAGES * STAGE_BYTES
     uint8_t *xs = stages + STAGES * STAGE_BYTES;                      // M * xstride
     float *xsum = reinterpret_cast<float *>(xs + p.M * xstride);      // [8][G]
-    float *red = xsum + 8 * p.G;                                      // [NPASS][8][16][8]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(red + NPASS * CWARPS * 128);
+    float *red = xsum + 8 * p.G;                                      // [2][NPASS][8][16][8]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(red + 2 * NPASS * CWARPS * 128);
     uint64_t *full = bars, *empty = bars + STAGES;
     volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 2 * STAGES);
 
@@ -114,11 +115,14 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                     const int s = it % STAGES;
                     if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY)) break;
                     uint8_t *sp = stages + s * STAGE_BYTES;
-                    mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+                    mbar_arrive_expect_tx(&full[s], NPASS * (C::W_BYTES + 2 * SB_BYTES));
 #pragma unroll
                     for (int ps = 0; ps < NPASS; ++ps) {
-                        uint8_t *pp = sp + ps * (C::W_BYTES + 2 * SB_BYTES);
-                        tma_load_3d(pp, ps ? &tm_w2 : &tm_w, &full[s], 0, st * 16, kc * RUNS);
+                        uint8_t *pp = sp + ps * PASS_BYTES;
+#pragma unroll
+                        for (int bx = 0; bx < WBOXES; ++bx)
+                            tma_load_2d(pp + bx * 2048, ps ? &tm_w2 : &tm_w, &full[s], (kc * KS * BITS / 8 + bx * 128) / 4,
+                                        st * 16);
                         tma_load_2d(pp + C::W_BYTES, ps ? &tm_s2 : &tm_s, &full[s], kc * GPS, st * 16);
                         tma_load_2d(pp + C::W_BYTES + SB_BYTES, ps ? &tm_b2 : &tm_b, &full[s], kc * GPS, st * 16);
                     }
@@ -130,7 +134,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
 
     // -------------------------------------------------------------------- consumers
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int tid = threadIdx.x;  // 0 .. 255
+    const int tid = threadIdx.x;  // consumer thread, 0 .. CWARPS * 32 - 1
     // x -> smem, permuted so that lane c of a warp reads its four bf16 pairs of a run in
     // one 16-byte load: Q4 pairs (0,4) (1,5) (2,6) (3,7), Q8 pairs (0,2) (1,3) (4,6) (5,7)
     // of the lane's 8 consecutive codes.
@@ -174,8 +178,9 @@ __global__ void __launch_bounds__(NTHREADS, 2)
 
     const int g = lane >> 2, c = lane & 3;
     const float cfold = BITS == 4 ? 128.f : 2176.f;  // offset folded back per group
+    const int lw = warp;                             // consumer warp
     constexpr int runs_per_group = GS / 32;
-    uint32_t it = 0;
+    uint32_t it = 0, strip_iter = 0;
     for (int st = blockIdx.x; st < nstrips; st += gridDim.x) {
         float acc[NPASS][4] = {};
         bool ok = true;
@@ -186,41 +191,89 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                 break;
             }
             const uint8_t *sp = stages + s * STAGE_BYTES;
+#ifdef QL_EXP_NOCOMP
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            continue;
+#endif
+            // ---- load phase: everything this warp needs from the stage goes to registers,
+            //      then the stage is released so the producer can refill it at once
+            constexpr int NG = 128 / GS;                 // groups covered by this warp's 4 runs
+            constexpr int NWW = BITS == 4 ? 1 : 2;       // words per lane per row per run
+            uint32_t wgv[NPASS][4][NWW], whv[NPASS][4][NWW];
+            uint16_t sgv[NPASS][NG], shv[NPASS][NG], bgv[NPASS][NG], bhv[NPASS][NG];
+            uint4 X[4];
+#pragma unroll
+            for (int rr = 0; rr < 4; ++rr) {
+                const int r = lw * 4 + rr;  // run within the stage
+                X[rr] = make_uint4(0, 0, 0, 0);  // tokens past M are zero
+                if (g < p.M) X[rr] = *reinterpret_cast<const uint4 *>(xs + g * xstride + ((kc * RUNS + r) * 4 + c) * 16);
+#pragma unroll
+                for (int ps = 0; ps < NPASS; ++ps) {
+                    const uint8_t *wp = sp + ps * PASS_BYTES;
+                    if constexpr (BITS == 4) {
+                        // box r/8 holds runs [8b, 8b+8) as 16 rows x 128 B; 16-byte chunk j of
+                        // row g sits at chunk j ^ (g % 8) (TMA 128-byte swizzle)
+                        const uint8_t *bp = wp + (r >> 3) * 2048 + g * 128 + (((r & 7) ^ g) << 4) + 4 * c;
+                        wgv[ps][rr][0] = *reinterpret_cast<const uint32_t *>(bp);
+                        whv[ps][rr][0] = *reinterpret_cast<const uint32_t *>(bp + 8 * 128);
+                    } else {
+                        // box r/4 holds runs [4b, 4b+4) (32 B each), swizzled as above
+                        const uint8_t *bp = wp + (r >> 2) * 2048 + g * 128 +
+                                            ((((2 * (r & 3)) + (c >> 1)) ^ g) << 4) + 8 * (c & 1);
+                        const uint2 a = *reinterpret_cast<const uint2 *>(bp);
+                        const uint2 bb = *reinterpret_cast<const uint2 *>(bp + 8 * 128);
+                        wgv[ps][rr][0] = a.x;
+                        wgv[ps][rr][NWW - 1] = a.y;
+                        whv[ps][rr][0] = bb.x;
+                        whv[ps][rr][NWW - 1] = bb.y;
+                    }
+                }
+            }
 #pragma unroll
             for (int ps = 0; ps < NPASS; ++ps) {
-                const uint8_t *wp = sp + ps * (C::W_BYTES + 2 * SB_BYTES);
-                const uint16_t *sc = reinterpret_cast<const uint16_t *>(wp + C::W_BYTES);
-                const uint16_t *bi = reinterpret_cast<const uint16_t *>(wp + C::W_BYTES + SB_BYTES);
+                const uint16_t *sc = reinterpret_cast<const uint16_t *>(sp + ps * PASS_BYTES + C::W_BYTES);
+                const uint16_t *bi = sc + SB_BYTES / 2;
+#pragma unroll
+                for (int q = 0; q < NG; ++q) {
+                    const int gl = lw * NG + q;  // group within the stage
+                    sgv[ps][q] = sc[g * GPS + gl];
+                    shv[ps][q] = sc[(g + 8) * GPS + gl];
+                    bgv[ps][q] = bi[g * GPS + gl];
+                    bhv[ps][q] = bi[(g + 8) * GPS + gl];
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            // ---- compute phase
+#pragma unroll
+            for (int ps = 0; ps < NPASS; ++ps) {
                 // two accumulators per nibble plane break the MMA dependency chain
                 float d[4] = {0.f, 0.f, 0.f, 0.f}, dh[4] = {0.f, 0.f, 0.f, 0.f};
                 float e[4] = {0.f, 0.f, 0.f, 0.f}, eh[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int rr = 0; rr < 4; ++rr) {
-                    const int r = warp * 4 + rr;          // run within the stage
-                    uint4 X = make_uint4(0, 0, 0, 0);  // tokens past M are zero
-                    if (g < p.M) X = *reinterpret_cast<const uint4 *>(xs + g * xstride + ((kc * RUNS + r) * 4 + c) * 16);
+                    const uint32_t *wg = wgv[ps][rr], *wh = whv[ps][rr];
                     if constexpr (BITS == 4) {
-                        const uint32_t wg = *reinterpret_cast<const uint32_t *>(wp + ((r * 16 + g) * 4 + c) * 4);
-                        const uint32_t wh = *reinterpret_cast<const uint32_t *>(wp + ((r * 16 + g + 8) * 4 + c) * 4);
-                        mma16816(d, nib2(wg, 0), nib2(wh, 0), nib2(wg, 1), nib2(wh, 1), X.x, X.y);
-                        mma16816(e, nib2(wg, 2), nib2(wh, 2), nib2(wg, 3), nib2(wh, 3), X.z, X.w);
+                        mma16816(d, nib2(wg[0], 0), nib2(wh[0], 0), nib2(wg[0], 1), nib2(wh[0], 1), X[rr].x, X[rr].y);
+                        mma16816(e, nib2(wg[0], 2), nib2(wh[0], 2), nib2(wg[0], 3), nib2(wh[0], 3), X[rr].z, X[rr].w);
                     } else {
-                        const uint2 wg = *reinterpret_cast<const uint2 *>(wp + ((r * 16 + g) * 8 + 2 * c) * 4);
-                        const uint2 wh = *reinterpret_cast<const uint2 *>(wp + ((r * 16 + g + 8) * 8 + 2 * c) * 4);
                         // low nibbles: (l0,l2) at shift 0, (l1,l3) at shift 8; high: 4, 12
-                        mma16816(d, nib2(wg.x, 0), nib2(wh.x, 0), nib2(wg.x, 2), nib2(wh.x, 2), X.x, X.y);
-                        mma16816(e, nib2(wg.y, 0), nib2(wh.y, 0), nib2(wg.y, 2), nib2(wh.y, 2), X.z, X.w);
-                        mma16816(dh, nib2(wg.x, 1), nib2(wh.x, 1), nib2(wg.x, 3), nib2(wh.x, 3), X.x, X.y);
-                        mma16816(eh, nib2(wg.y, 1), nib2(wh.y, 1), nib2(wg.y, 3), nib2(wh.y, 3), X.z, X.w);
+                        mma16816(d, nib2(wg[0], 0), nib2(wh[0], 0), nib2(wg[0], 2), nib2(wh[0], 2), X[rr].x, X[rr].y);
+                        mma16816(e, nib2(wg[NWW - 1], 0), nib2(wh[NWW - 1], 0), nib2(wg[NWW - 1], 2),
+                                 nib2(wh[NWW - 1], 2), X[rr].z, X[rr].w);
+                        mma16816(dh, nib2(wg[0], 1), nib2(wh[0], 1), nib2(wg[0], 3), nib2(wh[0], 3), X[rr].x, X[rr].y);
+                        mma16816(eh, nib2(wg[NWW - 1], 1), nib2(wh[NWW - 1], 1), nib2(wg[NWW - 1], 3),
+                                 nib2(wh[NWW - 1], 3), X[rr].z, X[rr].w);
                     }
-                    if ((r + 1) % runs_per_group == 0) {
+                    if ((rr + 1) % runs_per_group == 0) {
                         // fold the finished group: y += s D + (b - cfold s) X
-                        const int gl = (r * 32) / GS;                   // group within the stage
-                        const int gg = kc * GPS + gl;                   // global group
-                        const float sg = bf16lo((uint32_t)sc[g * GPS + gl]);
-                        const float sh = bf16lo((uint32_t)sc[(g + 8) * GPS + gl]);
-                        const float bg = bf16lo((uint32_t)bi[g * GPS + gl]) - cfold * sg;
-                        const float bh = bf16lo((uint32_t)bi[(g + 8) * GPS + gl]) - cfold * sh;
+                        const int q = rr / runs_per_group;
+                        const int gg = kc * GPS + lw * NG + q;  // global group
+                        const float sg = bf16lo((uint32_t)sgv[ps][q]);
+                        const float sh = bf16lo((uint32_t)shv[ps][q]);
+                        const float bg = bf16lo((uint32_t)bgv[ps][q]) - cfold * sg;
+                        const float bh = bf16lo((uint32_t)bhv[ps][q]) - cfold * sh;
                         const float x0 = gg < p.G ? xsum[(2 * c) * p.G + gg] : 0.f;
                         const float x1 = gg < p.G ? xsum[(2 * c + 1) * p.G + gg] : 0.f;
 #pragma unroll
@@ -242,28 +295,30 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                     }
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
         }
-        if (!ok) break;
-        // partial tiles of the 8 warps -> one 16 x 8 tile -> epilogue
+        // partial tiles of the 8 warps -> one 16 x 8 tile -> epilogue.  The buffer
+        // alternates per strip: the epilogue of strip i reads buffer i%2 while the
+        // other warps go on; the barrier of strip i+1 orders it before its reuse.
+        float *rb = red + (strip_iter & 1) * NPASS * CWARPS * 128;
+        ++strip_iter;
 #pragma unroll
         for (int ps = 0; ps < NPASS; ++ps) {
-            float *rp = red + (ps * CWARPS + warp) * 128;
+            float *rp = rb + (ps * CWARPS + warp) * 128;
             rp[g * 8 + 2 * c] = acc[ps][0];
             rp[g * 8 + 2 * c + 1] = acc[ps][1];
             rp[(g + 8) * 8 + 2 * c] = acc[ps][2];
             rp[(g + 8) * 8 + 2 * c + 1] = acc[ps][3];
         }
-        named_bar_sync(1, CWARPS * 32);
+        named_bar_sync(1, CWARPS * 32);  // every warp reaches it, aborted or not
+        if (!ok || *abort_flag) break;
         if (tid < 128) {
             const int r = tid >> 3, m = tid & 7, n = st * 16 + r;
             if (n < p.N && m < p.M) {
                 float a = 0.f, a2 = 0.f;
 #pragma unroll
                 for (int w = 0; w < CWARPS; ++w) {
-                    a += red[w * 128 + r * 8 + m];
-                    if (SWIGLU) a2 += red[(CWARPS + w) * 128 + r * 8 + m];
+                    a += rb[w * 128 + r * 8 + m];
+                    if (SWIGLU) a2 += rb[(CWARPS + w) * 128 + r * 8 + m];
                 }
                 if (p.lora_t) {
                     const __nv_bfloat16 *t = p.lora_t + (int64_t)m * p.rpad;
@@ -287,12 +342,12 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                 p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(v);
             }
         }
-        named_bar_sync(1, CWARPS * 32);
     }
 }
 
 static int make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, int rank, const uint64_t *dims,
-                    const uint64_t *strides_bytes, const uint32_t *box) {
+                    const uint64_t *strides_bytes, const uint32_t *box,
+                    CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE) {
     gemm::PFN_encodeTiled enc = gemm::get_encode();
     if (!enc) return fail(QL_ECUDA, "cuTensorMapEncodeTiled unavailable");
     cuuint64_t d[3], st[2];
@@ -303,7 +358,7 @@ static int make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, 
     }
     for (int i = 0; i + 1 < rank; ++i) st[i] = strides_bytes[i];
     CUresult r = enc(map, dt, (cuuint32_t)rank, const_cast<void *>(base), d, st, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(QL_ECUDA, "cuTensorMapEncodeTiled (gemv) failed (%d)", (int)r);
     return QL_OK;
 }
@@ -313,11 +368,11 @@ static int launch_t(const CUtensorMap *maps, const Params &p, cudaStream_t st) {
     using C = Cfg<BITS, SWIGLU>;
     auto kfn = qgemv_tma_kernel<BITS, SWIGLU, GS>;
     const int GPS = KS / p.gs;
-    const size_t stage_bytes = (size_t)C::NPASS * (C::W_BYTES + 2 * 16 * GPS * 2);
+    const size_t stage_bytes = (size_t)C::NPASS * ((C::W_BYTES + 2 * 16 * GPS * 2 + 1023) / 1024 * 1024);
     const int nruns = p.nks * RUNS;
     const size_t xstride = (size_t)nruns * 64 + ((nruns & 1) ? 0 : 64);
     const size_t smem = 1024 + C::STAGES * stage_bytes + (size_t)p.M * xstride + 8 * (size_t)p.G * 4 +
-                        (size_t)C::NPASS * CWARPS * 128 * 4 + 2 * C::STAGES * 8 + 16;
+                        2 * (size_t)C::NPASS * CWARPS * 128 * 4 + 2 * C::STAGES * 8 + 16;
     if (smem > 227 * 1024) return fail(QL_EUNSUPPORTED, "GEMV: K too large for the staged kernel");
     QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int dev = 0, sms = 148;
@@ -372,11 +427,13 @@ int launch_qgemv_tma(const void *x, int64_t M, int64_t K, const uint32_t *wq, co
     for (int ps = 0; ps < (sw ? 2 : 1); ++ps) {
         const uint32_t *w = ps ? wq2 : wq;
         const void *s = ps ? scales2 : scales, *b = ps ? biases2 : biases;
-        // W as (run words, row, run): strides row = K*bits/8 bytes, run = runw*4 bytes
-        const uint64_t wd[3] = {runw, (uint64_t)N, (uint64_t)(K / 32)};
-        const uint64_t ws[2] = {(uint64_t)K * bits / 8, runw * 4};
-        const uint32_t wb[3] = {(uint32_t)runw, 16, (uint32_t)RUNS};
-        if (int rc = make_map(&maps[3 * ps], CU_TENSOR_MAP_DATA_TYPE_UINT32, w, 3, wd, ws, wb)) return rc;
+        // W as words x rows; boxes of 128 B x 16 rows with the 128-byte swizzle
+        const uint64_t wd[2] = {(uint64_t)K * bits / 32, (uint64_t)N};
+        const uint64_t ws[1] = {(uint64_t)K * bits / 8};
+        const uint32_t wb[2] = {32, 16};
+        if (int rc = make_map(&maps[3 * ps], CU_TENSOR_MAP_DATA_TYPE_UINT32, w, 2, wd, ws, wb,
+                              CU_TENSOR_MAP_SWIZZLE_128B))
+            return rc;
         const uint64_t sd[2] = {(uint64_t)p.G, (uint64_t)N};
         const uint64_t ss[1] = {(uint64_t)p.G * 2};
         const uint32_t sbx[2] = {(uint32_t)(KS / gs), 16};
