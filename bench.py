@@ -303,10 +303,18 @@ def run_ours(args):
     # clocks are sampled from here to the end of the timed region; a ~1 s untimed soak
     # first brings the GPU to its steady (power-capped) clock so the samples describe load
     clocks = ClockSampler(local) if rank == 0 else None
-    t_soak = time.perf_counter()
-    while time.perf_counter() - t_soak < 1.0:
+    # ~1 s of untimed soak; the step count is agreed across ranks (every rank must run the
+    # same number of collectives)
+    t_w = time.perf_counter()
+    for _ in range(3):
         step()
-        torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    n_soak = torch.tensor([int(1.0 / max((time.perf_counter() - t_w) / 3, 1e-4))], device=dev)
+    if world > 1:
+        dist.all_reduce(n_soak, op=dist.ReduceOp.MAX)
+    for _ in range(int(n_soak.item())):
+        step()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
