@@ -277,22 +277,38 @@ def run_ours(args):
     torch.cuda.synchronize()
 
     evs = []  # (name, start, end) of every GEMM launch in the timed region
+    # N > 1: each row-parallel output is all-reduced on a second stream so the collective
+    # overlaps the next GEMM (the out-projection's with MLP-up, MLP-down's with the next
+    # step's QKV); the GEMMs then leave `comm_sms` SMs free for the NCCL kernels.
+    main = torch.cuda.current_stream(dev)
+    comm = torch.cuda.Stream(dev) if world > 1 else None
+    ar_done = {n: torch.cuda.Event() for n in lin}
+    max_ctas = 0
+    if world > 1:
+        max_ctas = torch.cuda.get_device_properties(dev).multi_processor_count - args.comm_sms
 
-    def step(record=False, xin=None):
+    def step(record=False, xin=None, need_result=False):
         xin = x if xin is None else xin
         for name in ("qkv", "out", "up", "down"):
             l = lin[name]
             inp = out["up"] if name == "down" else xin
+            if world > 1 and l["style"] == "row":
+                main.wait_event(ar_done[name])  # previous step's reduction of this buffer
             if record:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
             qlinear.quantized_matmul(inp, l["wq"], l["s"], l["b"], True, gs, bits, bias=l["bias"], act=l["act"],
-                                     kernel=qlinear.KERNEL_GEMM, out=out[name])
+                                     kernel=qlinear.KERNEL_GEMM, out=out[name], max_ctas=max_ctas)
             if record:
                 e1.record()
                 evs.append((name, e0, e1))
             if world > 1 and l["style"] == "row":
-                dist.all_reduce(out[name])
+                comm.wait_stream(main)
+                with torch.cuda.stream(comm):
+                    dist.all_reduce(out[name])
+                    ar_done[name].record(comm)
+        if world > 1 and need_result:
+            main.wait_event(ar_done["down"])  # the block output is complete
         return out["down"]
 
     for _ in range(max(args.warmup, 3)):
@@ -373,7 +389,7 @@ def run_ours(args):
     t0.record()
     for _ in range(args.steps):
         xd.copy_(xh, non_blocking=True)
-        y = step(xin=xd)
+        y = step(xin=xd, need_result=True)
         yh.copy_(y, non_blocking=True)
     t1.record()
     torch.cuda.synchronize()
@@ -403,6 +419,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip cpu_baseline and decode_gemv")
+    ap.add_argument("--comm-sms", type=int, default=8, help="SMs left to NCCL when N > 1")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

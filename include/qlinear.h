@@ -82,6 +82,8 @@ typedef struct {
     void *workspace;
     size_t workspace_bytes;
     int kernel;                /* ql_kernel (QL_KERNEL_AUTO unless testing a path)     */
+    int max_ctas;              /* GEMM: cap on resident CTAs (0 = one per SM); leaves
+                                  SMs free for a collective running alongside          */
 } ql_epilogue;
 
 /* Library version (major*10000 + minor*100 + patch). */

@@ -38,7 +38,7 @@ int launch_qgemv(const void *, int64_t, int64_t, const uint32_t *, const void *,
                  const void *, int, const void *, const void *, int64_t, void *, cudaStream_t);
 int launch_qgemm_sm100(const void *, int64_t, int64_t, const uint32_t *, const void *, const void *,
                        const uint32_t *, const void *, const void *, int64_t, int, int, const void *,
-                       const void *, int, const void *, const void *, int64_t, void *, int, cudaStream_t);
+                       const void *, int, const void *, const void *, int64_t, void *, int, int, cudaStream_t);
 int launch_qmm_generic(const void *, int, int64_t, int64_t, const uint32_t *, const void *,
                        const void *, const uint32_t *, const void *, const void *, int, int64_t, int,
                        int, const void *, const void *, int, const void *, const void *, int64_t,
@@ -191,7 +191,7 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
                             bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y, st);
     return launch_qgemm_sm100(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size,
                               bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y,
-                              kernel == QL_KERNEL_GEMM_PAIR ? 2 : 1, st);
+                              kernel == QL_KERNEL_GEMM_PAIR ? 2 : 1, e.max_ctas, st);
 }
 
 }  // extern "C"

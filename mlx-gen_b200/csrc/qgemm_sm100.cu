@@ -540,7 +540,7 @@ static int make_map_2d(CUtensorMap *map, CUtensorMapDataType dt, int elem_bytes,
 
 template <int BITS, bool SWIGLU, int CG>
 static int launch_t(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mw2,
-                    const CUtensorMap &mt, const Params &p, cudaStream_t st) {
+                    const CUtensorMap &mt, const Params &p, int max_ctas, cudaStream_t st) {
     using C = Cfg<BITS, CG>;
     auto kfn = qgemm_kernel<BITS, SWIGLU, CG>;
     static bool configured = false;  // per template instance; attribute is per-function
@@ -574,7 +574,8 @@ static int launch_t(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensor
         max_clusters = mc;
         if (getenv("QL_DEBUG")) fprintf(stderr, "qgemm CG=%d: %d resident clusters, smem %d\n", CG, mc, C::SMEM_TOTAL);
     }
-    const int clusters = tiles < max_clusters ? tiles : max_clusters;
+    int clusters = tiles < max_clusters ? tiles : max_clusters;
+    if (max_ctas > 0 && clusters > max_ctas / CG) clusters = max_ctas / CG > 0 ? max_ctas / CG : 1;
     cfg.gridDim = dim3((unsigned)(clusters * CG));
     QL_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, mx, mw, mw2, mt, p));
     return QL_OK;
@@ -594,7 +595,7 @@ int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, 
                        const void *biases, const uint32_t *wq2, const void *scales2,
                        const void *biases2, int64_t N, int gs, int bits, const void *bias,
                        const void *bias2, int act, const void *lora_t, const void *lora_b,
-                       int64_t rank, void *y, int cg, cudaStream_t st) {
+                       int64_t rank, void *y, int cg, int max_ctas, cudaStream_t st) {
     using namespace gemm;
     const bool swiglu = act == QL_ACT_SWIGLU;
     const int wrows = (swiglu ? 64 : BW) * cg;  // output columns per tile
@@ -645,12 +646,12 @@ int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, 
     }
     if (cg == 2) {
         if (bits == 4)
-            return swiglu ? launch_t<4, true, 2>(mx, mw, mw2, mt, p, st) : launch_t<4, false, 2>(mx, mw, mw2, mt, p, st);
-        return swiglu ? launch_t<8, true, 2>(mx, mw, mw2, mt, p, st) : launch_t<8, false, 2>(mx, mw, mw2, mt, p, st);
+            return swiglu ? launch_t<4, true, 2>(mx, mw, mw2, mt, p, max_ctas, st) : launch_t<4, false, 2>(mx, mw, mw2, mt, p, max_ctas, st);
+        return swiglu ? launch_t<8, true, 2>(mx, mw, mw2, mt, p, max_ctas, st) : launch_t<8, false, 2>(mx, mw, mw2, mt, p, max_ctas, st);
     }
     if (bits == 4)
-        return swiglu ? launch_t<4, true, 1>(mx, mw, mw2, mt, p, st) : launch_t<4, false, 1>(mx, mw, mw2, mt, p, st);
-    return swiglu ? launch_t<8, true, 1>(mx, mw, mw2, mt, p, st) : launch_t<8, false, 1>(mx, mw, mw2, mt, p, st);
+        return swiglu ? launch_t<4, true, 1>(mx, mw, mw2, mt, p, max_ctas, st) : launch_t<4, false, 1>(mx, mw, mw2, mt, p, max_ctas, st);
+    return swiglu ? launch_t<8, true, 1>(mx, mw, mw2, mt, p, max_ctas, st) : launch_t<8, false, 1>(mx, mw, mw2, mt, p, max_ctas, st);
 }
 
 }  // namespace ql

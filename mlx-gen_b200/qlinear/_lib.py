@@ -67,6 +67,7 @@ class Epilogue(C.Structure):
         ("workspace", C.c_void_p),
         ("workspace_bytes", C.c_size_t),
         ("kernel", C.c_int),
+        ("max_ctas", C.c_int),
     ]
 
 

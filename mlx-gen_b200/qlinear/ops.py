@@ -102,7 +102,8 @@ def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, bi
                      bias: Optional[torch.Tensor] = None, act: Optional[str] = None,
                      up: Optional[Sequence[Optional[torch.Tensor]]] = None,
                      lora: Optional[tuple] = None, workspace: Optional[torch.Tensor] = None,
-                     kernel: int = KERNEL_AUTO, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     kernel: int = KERNEL_AUTO, out: Optional[torch.Tensor] = None,
+                     max_ctas: int = 0) -> torch.Tensor:
     """``y = x . dequant(W)^T`` (+ fused epilogue), like ``mlx_rs::ops::quantized_matmul``
     with ``transpose=true`` followed by the ops the reference runs after it.
 
@@ -152,6 +153,7 @@ def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, bi
         ep.workspace = workspace.data_ptr()
         ep.workspace_bytes = workspace.numel() * workspace.element_size()
     ep.kernel = kernel
+    ep.max_ctas = max_ctas
     check(lib().ql_quantized_matmul(_ptr(x2), dtype_code(x2), M, K, _ptr(wq.contiguous()),
                                     _ptr(scales.contiguous()), _ptr(biases.contiguous()),
                                     dtype_code(scales), N, group_size, bits, 1, C.byref(ep), _ptr(y),
