@@ -194,11 +194,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     uint8_t *ws = smem + C::SMEM_W + s * C::W_STAGE_BYTES;
                     const bool wstep = kt < p.ktw;
                     // x half (or LoRA T half): counted on the leader's xfull[s]
+#ifdef QL_EXP_NOX
+                    if (rank == 0) mbar_arrive(&xfull[s]);
+#else
                     if (rank == 0) mbar_arrive_expect_tx(&xfull[s], CG * C::X_STAGE_BYTES);
+#endif
                     const CUtensorMap *xm = wstep ? &tm_x : &tm_t;
                     const int xk = wstep ? kt * BK : (kt - p.ktw) * BK;
+#ifdef QL_EXP_NOX
+                    (void)xm; (void)xk; (void)xrow; (void)xs;
+#else
                     if (CG == 2) tma_load_2d_pair(xs, xm, leader(&xfull[s]), xk, xrow);
                     else tma_load_2d(xs, xm, &xfull[s], xk, xrow);
+#endif
                     // packed W rows of this CTA: counted on the local wfull[s]
                     if (wstep) {
                         mbar_arrive_expect_tx(&wfull[s], C::W_STAGE_BYTES);
@@ -470,8 +478,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     r[c] = lo | (hi << 16);
                 }
             }
+#ifndef QL_EXP_NOWST
             tmem_st32(taddr_lane + j * 32, r);
             tmem_st_wait();
+#else
+            if (r[0] == 0x12345u && r[31] == 7u) tmem_st32(taddr_lane + j * 32, r);
+#endif
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {

@@ -423,7 +423,6 @@ int launch_qgemv_tma(const void *x, int64_t M, int64_t K, const uint32_t *wq, co
     p.y = (__nv_bfloat16 *)y;
 
     CUtensorMap maps[6];
-    const uint64_t runw = (uint64_t)bits;  // words per 32-code run
     for (int ps = 0; ps < (sw ? 2 : 1); ++ps) {
         const uint32_t *w = ps ? wq2 : wq;
         const void *s = ps ? scales2 : scales, *b = ps ? biases2 : biases;
