@@ -53,6 +53,9 @@ struct Cfg {
 
 __device__ __forceinline__ void mma16816(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
+#ifdef QL_EXP_NOMMA
+    d[0] += __uint_as_float(a0 ^ a1 ^ b0); d[1] += __uint_as_float(a2 ^ a3 ^ b1); return;
+#endif
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
         "{%8, %9}, {%0, %1, %2, %3};"
@@ -62,6 +65,9 @@ __device__ __forceinline__ void mma16816(float d[4], uint32_t a0, uint32_t a1, u
 
 // bf16x2 (128 + code_lo, 128 + code_hi) from the nibbles at bit 4j and 16 + 4j
 __device__ __forceinline__ uint32_t nib2(uint32_t w, int j) {
+#ifdef QL_EXP_NONIB
+    return w + j;
+#endif
     return ((w >> (4 * j)) & 0x000f000fu) | 0x43004300u;
 }
 
@@ -245,54 +251,70 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
-            // ---- compute phase
+#ifdef QL_EXP_LOADONLY
+#pragma unroll
+            for (int rr = 0; rr < 4; ++rr) acc[0][0] += __uint_as_float(wgv[0][rr][0] ^ whv[0][rr][0] ^ X[rr].x ^ sgv[0][0] ^ bhv[0][NG - 1]);
+            continue;
+#endif
+            // ---- compute phase.  Every MMA of the stage first (independent accumulators:
+            //      per group, per plane -- Q4 halves a/b, Q8 low/high nibbles -- and, for
+            //      one group per warp, per run parity), runs of different groups interleaved;
+            //      then one fold per group.
+            constexpr int RP = NG == 1 ? 2 : 1;
+            constexpr int ORD[4] = {0, NG == 2 ? 2 : 1, NG == 2 ? 1 : 2, 3};
 #pragma unroll
             for (int ps = 0; ps < NPASS; ++ps) {
-                // two accumulators per nibble plane break the MMA dependency chain
-                float d[4] = {0.f, 0.f, 0.f, 0.f}, dh[4] = {0.f, 0.f, 0.f, 0.f};
-                float e[4] = {0.f, 0.f, 0.f, 0.f}, eh[4] = {0.f, 0.f, 0.f, 0.f};
+                float ac[NG][2][RP][4];
 #pragma unroll
-                for (int rr = 0; rr < 4; ++rr) {
+                for (int q = 0; q < NG; ++q)
+#pragma unroll
+                    for (int m = 0; m < 2; ++m)
+#pragma unroll
+                        for (int t = 0; t < RP; ++t)
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) ac[q][m][t][i] = 0.f;
+#pragma unroll
+                for (int oi = 0; oi < 4; ++oi) {
+                    const int rr = ORD[oi];
+                    const int q = rr / runs_per_group, t = rr % RP;
                     const uint32_t *wg = wgv[ps][rr], *wh = whv[ps][rr];
                     if constexpr (BITS == 4) {
-                        mma16816(d, nib2(wg[0], 0), nib2(wh[0], 0), nib2(wg[0], 1), nib2(wh[0], 1), X[rr].x, X[rr].y);
-                        mma16816(e, nib2(wg[0], 2), nib2(wh[0], 2), nib2(wg[0], 3), nib2(wh[0], 3), X[rr].z, X[rr].w);
+                        mma16816(ac[q][0][t], nib2(wg[0], 0), nib2(wh[0], 0), nib2(wg[0], 1), nib2(wh[0], 1), X[rr].x, X[rr].y);
+                        mma16816(ac[q][1][t], nib2(wg[0], 2), nib2(wh[0], 2), nib2(wg[0], 3), nib2(wh[0], 3), X[rr].z, X[rr].w);
                     } else {
                         // low nibbles: (l0,l2) at shift 0, (l1,l3) at shift 8; high: 4, 12
-                        mma16816(d, nib2(wg[0], 0), nib2(wh[0], 0), nib2(wg[0], 2), nib2(wh[0], 2), X[rr].x, X[rr].y);
-                        mma16816(e, nib2(wg[NWW - 1], 0), nib2(wh[NWW - 1], 0), nib2(wg[NWW - 1], 2),
+                        mma16816(ac[q][0][t], nib2(wg[0], 0), nib2(wh[0], 0), nib2(wg[0], 2), nib2(wh[0], 2), X[rr].x, X[rr].y);
+                        mma16816(ac[q][1][t], nib2(wg[0], 1), nib2(wh[0], 1), nib2(wg[0], 3), nib2(wh[0], 3), X[rr].x, X[rr].y);
+                        mma16816(ac[q][0][t], nib2(wg[NWW - 1], 0), nib2(wh[NWW - 1], 0), nib2(wg[NWW - 1], 2),
                                  nib2(wh[NWW - 1], 2), X[rr].z, X[rr].w);
-                        mma16816(dh, nib2(wg[0], 1), nib2(wh[0], 1), nib2(wg[0], 3), nib2(wh[0], 3), X[rr].x, X[rr].y);
-                        mma16816(eh, nib2(wg[NWW - 1], 1), nib2(wh[NWW - 1], 1), nib2(wg[NWW - 1], 3),
+                        mma16816(ac[q][1][t], nib2(wg[NWW - 1], 1), nib2(wh[NWW - 1], 1), nib2(wg[NWW - 1], 3),
                                  nib2(wh[NWW - 1], 3), X[rr].z, X[rr].w);
                     }
-                    if ((rr + 1) % runs_per_group == 0) {
-                        // fold the finished group: y += s D + (b - cfold s) X
-                        const int q = rr / runs_per_group;
-                        const int gg = kc * GPS + lw * NG + q;  // global group
-                        const float sg = bf16lo((uint32_t)sgv[ps][q]);
-                        const float sh = bf16lo((uint32_t)shv[ps][q]);
-                        const float bg = bf16lo((uint32_t)bgv[ps][q]) - cfold * sg;
-                        const float bh = bf16lo((uint32_t)bhv[ps][q]) - cfold * sh;
-                        const float x0 = gg < p.G ? xsum[(2 * c) * p.G + gg] : 0.f;
-                        const float x1 = gg < p.G ? xsum[(2 * c + 1) * p.G + gg] : 0.f;
+                }
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            d[i] += e[i];
-                            e[i] = 0.f;
-                            if (BITS == 8) {
-                                d[i] = fmaf(16.f, dh[i] + eh[i], d[i]);
-                                dh[i] = 0.f;
-                                eh[i] = 0.f;
-                            }
+                for (int q = 0; q < NG; ++q) {
+                    // fold the group: y += s D + (b - cfold s) X
+                    const int gg = kc * GPS + lw * NG + q;  // global group
+                    const float sg = bf16lo((uint32_t)sgv[ps][q]);
+                    const float sh = bf16lo((uint32_t)shv[ps][q]);
+                    const float bg = bf16lo((uint32_t)bgv[ps][q]) - cfold * sg;
+                    const float bh = bf16lo((uint32_t)bhv[ps][q]) - cfold * sh;
+                    const float x0 = gg < p.G ? xsum[(2 * c) * p.G + gg] : 0.f;
+                    const float x1 = gg < p.G ? xsum[(2 * c + 1) * p.G + gg] : 0.f;
+                    float d[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        float lo = ac[q][0][0][i], hi = ac[q][1][0][i];
+                        if (RP == 2) {
+                            lo += ac[q][0][RP - 1][i];
+                            hi += ac[q][1][RP - 1][i];
                         }
-                        acc[ps][0] += fmaf(sg, d[0], bg * x0);
-                        acc[ps][1] += fmaf(sg, d[1], bg * x1);
-                        acc[ps][2] += fmaf(sh, d[2], bh * x0);
-                        acc[ps][3] += fmaf(sh, d[3], bh * x1);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) d[i] = 0.f;
+                        d[i] = BITS == 8 ? fmaf(16.f, hi, lo) : lo + hi;
                     }
+                    acc[ps][0] += fmaf(sg, d[0], bg * x0);
+                    acc[ps][1] += fmaf(sg, d[1], bg * x1);
+                    acc[ps][2] += fmaf(sh, d[2], bh * x0);
+                    acc[ps][3] += fmaf(sh, d[3], bh * x1);
                 }
             }
         }
