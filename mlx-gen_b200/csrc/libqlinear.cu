@@ -7,6 +7,7 @@
 #include "qgemm_sm100.cu"
 #include "qgemv.cu"
 #include "qgemv_tma.cu"
+#include "qgemv_tc.cu"
 #include "qmm_generic.cu"
 #include "quantize.cu"
 #include "noalloc.cu"

@@ -279,12 +279,29 @@ int launch_qgemv_tma(const void *x, int64_t M, int64_t K, const uint32_t *wq, co
                      int64_t N, int gs, int bits, const void *bias, const void *bias2, int act,
                      const void *lora_t, const void *lora_b, int64_t rank, void *y, cudaStream_t st);
 
+bool qgemv_tc_supported(int64_t M, int64_t K, int gs, int bits, const void *x, bool lora);
+int launch_qgemv_tc(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales, const void *biases,
+                    const uint32_t *wq2, const void *scales2, const void *biases2, int64_t N, int gs, int bits,
+                    const void *bias, const void *bias2, int act, void *y, cudaStream_t st);
+
+static bool all_aligned16(std::initializer_list<const void *> ps) {
+    for (const void *p : ps)
+        if (p && reinterpret_cast<uintptr_t>(p) % 16) return false;
+    return true;
+}
+
 int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales,
                  const void *biases, const uint32_t *wq2, const void *scales2, const void *biases2,
                  int64_t N, int gs, int bits, const void *bias, const void *bias2, int act,
                  const void *lora_t, const void *lora_b, int64_t rank, void *y, cudaStream_t st) {
-    // the TMA-fed kernel (qgemv_tma.cu) whenever the shape allows it
-    static const bool force_regs = getenv("QL_GEMV_REGS") != nullptr;  // profiling switch
+    // the tcgen05 kernel (qgemv_tc.cu) when the shape allows it, else the TMA-fed
+    // mma.sync kernel (qgemv_tma.cu), else the register-fed one below
+    static const bool force_regs = getenv("QL_GEMV_REGS") != nullptr;  // profiling switches
+    static const bool force_mma = getenv("QL_GEMV_MMA") != nullptr;
+    if (!force_regs && !force_mma && qgemv_tc_supported(M, K, gs, bits, x, lora_t != nullptr) &&
+        all_aligned16({scales, biases, scales2, biases2}))
+        return launch_qgemv_tc(x, M, K, wq, scales, biases, wq2, scales2, biases2, N, gs, bits, bias, bias2, act, y,
+                               st);
     if (!force_regs && qgemv_tma_supported(M, K, gs))
         return launch_qgemv_tma(x, M, K, wq, scales, biases, wq2, scales2, biases2, N, gs, bits, bias, bias2, act,
                                 lora_t, lora_b, rank, y, st);

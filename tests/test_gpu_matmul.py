@@ -175,3 +175,42 @@ def test_gemv_tma_epilogues(dev, bits, epi):
     torch.cuda.synchronize()
     assert qlinear.device_error() == 0
     assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), what=f"gemv-tma {epi}", **tol)
+
+
+@pytest.mark.parametrize("bits,gs,M,N,K,epi", [
+    (4, 64, 1, 19300, 1024, None),         # more tiles than SMs, ragged last tile
+    (8, 128, 3, 300, 4096, None),          # Q8, 2 groups per stage, K split over a cluster
+    (4, 128, 8, 128, 8192, "bias_gelu"),   # one tile: the widest K split
+    (8, 64, 2, 500, 3072, "swiglu"),
+    (4, 64, 1, 3072, 3072, "bias"),        # decode-sized projection
+    (4, 64, 6, 1000, 512, "gelu_erf"),     # one stage per row tile
+])
+def test_gemv_tc_shapes(dev, bits, gs, M, N, K, epi):
+    """The tcgen05 GEMV (M <= 8, group size 64/128, K a whole number of 256-byte row
+    stages): tile counts above the SM count, K split across a cluster, every epilogue.
+    Like the mma.sync GEMV it uses the weights exactly while the oracle rounds them to bf16
+    first, so activation epilogues get relative L2 6e-3."""
+    rng, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 31 + M + bits)
+    tol = {}
+    if epi == "swiglu":
+        w3 = rand_bf16((N, K), 0.02, rng)
+        wq3, s3, b3 = O.quantize(w3, gs, bits)
+        bias3 = rand_bf16((N,), 0.2, rng)
+        y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, act="swiglu",
+                                     up=(np2t(wq3, dev), np2t(s3, dev), np2t(b3, dev), np2t(bias3, dev)),
+                                     kernel=GEMV)
+        ref = O.swiglu(O.quantized_matmul(x, wq, s, b, gs, bits),
+                       O.quantized_matmul(x, wq3, s3, b3, gs, bits, bias=bias3))
+        tol = dict(ulps=4, rl2=6e-3)
+    else:
+        bias = rand_bf16((N,), 0.2, rng) if epi else None
+        act = {None: None, "bias": None, "bias_gelu": "gelu_tanh", "gelu_erf": "gelu"}[epi]
+        oact = {None: O.ACT_NONE, "gelu_tanh": O.ACT_GELU_TANH, "gelu": O.ACT_GELU_ERF}[act]
+        y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, bias=None if bias is None else np2t(bias, dev),
+                                     act=act, kernel=GEMV)
+        ref = O.quantized_matmul(x, wq, s, b, gs, bits, bias=bias, act=oact)
+        if act:
+            tol = dict(ulps=4, rl2=6e-3)
+    torch.cuda.synchronize()
+    assert qlinear.device_error() == 0
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), what=f"gemv-tc {bits} {gs} {M}x{N}x{K} {epi}", **tol)
