@@ -58,6 +58,8 @@ typedef enum {
     QL_KERNEL_GEMV = 2,    /* M <= 8, bf16 x and bf16 scales                     */
     QL_KERNEL_GEMM = 3,    /* tcgen05 / TMEM GEMM, one CTA per MMA (cta_group::1) */
     QL_KERNEL_GEMM_PAIR = 4, /* the same GEMM on CTA pairs (cta_group::2); slower today */
+    QL_KERNEL_GEMV_TC = 5, /* the tcgen05 GEMV alone (M <= 8, no LoRA, group 64/128 or Q8/32;
+                              QL_EUNSUPPORTED otherwise); QL_KERNEL_GEMV picks it for wide N */
 } ql_kernel;
 
 /* Fused epilogue and options of ql_quantized_matmul.  Zero-initialise, then set

@@ -36,6 +36,10 @@ int launch_dequantize(const int64_t *, int64_t, int64_t, int64_t, int, int, cons
 int launch_qgemv(const void *, int64_t, int64_t, const uint32_t *, const void *, const void *,
                  const uint32_t *, const void *, const void *, int64_t, int, int, const void *,
                  const void *, int, const void *, const void *, int64_t, void *, cudaStream_t);
+bool qgemv_tc_supported(int64_t, int64_t, int, int, const void *, bool);
+int launch_qgemv_tc(const void *, int64_t, int64_t, const uint32_t *, const void *, const void *, const uint32_t *,
+                    const void *, const void *, int64_t, int, int, const void *, const void *, int, void *,
+                    cudaStream_t);
 int launch_qgemm_sm100(const void *, int64_t, int64_t, const uint32_t *, const void *, const void *,
                        const uint32_t *, const void *, const void *, int64_t, int, int, const void *,
                        const void *, int, const void *, const void *, int64_t, void *, int, int, cudaStream_t);
@@ -168,8 +172,16 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
     if (kernel == QL_KERNEL_AUTO) kernel = !tc_dtypes ? QL_KERNEL_GENERIC : (M <= 8 ? QL_KERNEL_GEMV : QL_KERNEL_GEMM);
     if (kernel != QL_KERNEL_GENERIC && !tc_dtypes)
         return fail(QL_EUNSUPPORTED, "tensor-core kernels need bf16 x, scales and y");
-    if (kernel == QL_KERNEL_GEMV && M > 8) return fail(QL_EUNSUPPORTED, "GEMV kernel needs M <= 8");
-    if (kernel < QL_KERNEL_AUTO || kernel > QL_KERNEL_GEMM_PAIR) return fail(QL_EINVAL_ARG, "unknown kernel %d", kernel);
+    if ((kernel == QL_KERNEL_GEMV || kernel == QL_KERNEL_GEMV_TC) && M > 8)
+        return fail(QL_EUNSUPPORTED, "GEMV kernel needs M <= 8");
+    if (kernel < QL_KERNEL_AUTO || kernel > QL_KERNEL_GEMV_TC) return fail(QL_EINVAL_ARG, "unknown kernel %d", kernel);
+    if (kernel == QL_KERNEL_GEMV_TC) {
+        if (lora || !qgemv_tc_supported(M, K, group_size, bits, x, false) ||
+            !aligned16(scales) || !aligned16(biases) || (swiglu && (!aligned16(e.scales_up) || !aligned16(e.biases_up))))
+            return fail(QL_EUNSUPPORTED, "tcgen05 GEMV: unsupported shape, group size or LoRA");
+        return launch_qgemv_tc(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size, bits,
+                               e.bias, e.bias_up, e.act, y, st);
+    }
 
     if (kernel == QL_KERNEL_GENERIC)
         return launch_qmm_generic(x, x_dtype, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up,

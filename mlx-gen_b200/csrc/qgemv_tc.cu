@@ -355,6 +355,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int upt = nst * UPS;  // units per tile
             uint32_t u = 0;
             bool ok = true;
+#ifdef QL_EXP_PRODONLY
+            ok = false;
+#endif
             for (int tile = cluster; tile < p.ntiles && ok; tile += nclusters) {
 #pragma unroll 1
                 for (int uu = 0; uu < upt; ++uu, ++u) {
@@ -372,7 +375,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     for (int ks = 0; ks < KPU; ++ks) {
                         const int c = uu * UCH + ks / 4;  // chunk of the slice = 128-K block of B
                         const uint64_t bdesc = umma_desc_k_sw128(bxs + c * 2048) + 2 * (ks % 4);
+#ifndef QL_EXP_NOMMA
                         tc_mma_ts_f8(dbase + (ks / KPG) * 16, abase + ks * 8, bdesc, idesc, (ks % KPG) ? 1u : 0u);
+#else
+                        (void)bdesc; (void)dbase; (void)abase;
+#endif
                     }
                     tc_commit(&udone[us]);
                 }
@@ -392,11 +399,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     ok = false;
                     break;
                 }
+#ifdef QL_EXP_PRODONLY
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+                continue;
+#endif
                 const uint8_t *wrow = smem + s * W_BYTES + row * 128;
-#pragma unroll
-                for (int j = 0; j < UPS; ++j, ++u) {
-                    const int us = u % AU;
-                    uint4 wv[4 * UCH];
+                // the loads of unit j + 1 are issued while unit j's TMEM store is in flight
+                uint4 wv[4 * UCH];
+                auto load_unit = [&](int j) {
 #pragma unroll
                     for (int ch = 0; ch < UCH; ++ch) {
                         const int c = j * UCH + ch;  // chunk of the stage: 64 bytes of the row
@@ -406,12 +417,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             wv[4 * ch + i] =
                                 *reinterpret_cast<const uint4 *>(wrow + h * (ROWS * 128) + (((j0 + i) ^ (row & 7)) << 4));
                     }
+                };
+                load_unit(0);
+#pragma unroll
+                for (int j = 0; j < UPS; ++j, ++u) {
+                    const int us = u % AU;
                     if (!TR_WAIT(warp == 4 ? 6 : 15, mbar_wait(&udone[us], ((u / AU) & 1) ^ 1, abort_flag,
                                                                DEV_ERR_TIMEOUT_EMPTY))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
+#ifndef QL_EXP_NODQ
 #pragma unroll
                     for (int ch = 0; ch < UCH; ++ch) {
                         uint32_t r[32];
@@ -427,13 +444,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         }
                         tmem_st32(taddr + us * 32 * UCH + ch * 32, r);
                     }
+#else
+                    if (wv[0].x == 0x12345678u && wv[1].y == 0x9abcdef0u) mbar_arrive(&afull[us]);  // keep the loads
+#endif
+                    if (j + 1 < UPS) {
+                        load_unit(j + 1);
+                    } else {
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&empty[s]);  // the stage's weights are all in registers
+                    }
                     tmem_st_wait();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&afull[us]);
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
             }
         }
     } else if (warp >= 8) {
@@ -457,6 +481,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     break;
                 }
                 const uint8_t *sp = sb_ring + b * SB_SLOT;
+#ifdef QL_EXP_PRODONLY
+                u += upb;
+                mbar_arrive(&sbempty[b]);
+                continue;
+#endif
 #pragma unroll 1
                 for (int uu = ub + fset; uu < ub + upb; uu += 2) {
                     const uint32_t uc = u + (uu - ub);  // unit counter of this unit
@@ -468,6 +497,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                     tc_fence_after();
                     uint32_t v[16 * GPUN];
+#ifdef QL_EXP_NOFOLD
+                    if (lane == 0) mbar_arrive(&dfree[us]);
+                    continue;
+#endif
                     if (GPUN == 2)
                         tmem_ld32(taddr + us * 32, v);
                     else
@@ -675,9 +708,10 @@ static int launch_t(const CUtensorMap *maps, const Params &p, size_t smem, int s
     cfg.blockDim = dim3(NTHREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
+    static const bool no_pdl = getenv("QL_GEMV_NOPDL") != nullptr;  // tuning switch
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[0].val.programmaticStreamSerializationAllowed = no_pdl ? 0 : 1;
     int na = 1;
     if (p.split > 1) {
         attr[1].id = cudaLaunchAttributeClusterDimension;

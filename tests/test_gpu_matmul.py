@@ -12,6 +12,7 @@ from helpers import assert_bf16_close, np2t, rand_bf16, t2np
 
 pytestmark = pytest.mark.gpu
 GEMV, GEMM, GENERIC = qlinear.KERNEL_GEMV, qlinear.KERNEL_GEMM, qlinear.KERNEL_GENERIC
+GEMV_TC = qlinear.KERNEL_GEMV_TC
 GEMM2 = qlinear.KERNEL_GEMM_PAIR
 
 
@@ -198,7 +199,7 @@ def test_gemv_tc_shapes(dev, bits, gs, M, N, K, epi):
         bias3 = rand_bf16((N,), 0.2, rng)
         y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, act="swiglu",
                                      up=(np2t(wq3, dev), np2t(s3, dev), np2t(b3, dev), np2t(bias3, dev)),
-                                     kernel=GEMV)
+                                     kernel=GEMV_TC)
         ref = O.swiglu(O.quantized_matmul(x, wq, s, b, gs, bits),
                        O.quantized_matmul(x, wq3, s3, b3, gs, bits, bias=bias3))
         tol = dict(ulps=4, rl2=6e-3)
@@ -207,10 +208,33 @@ def test_gemv_tc_shapes(dev, bits, gs, M, N, K, epi):
         act = {None: None, "bias": None, "bias_gelu": "gelu_tanh", "gelu_erf": "gelu"}[epi]
         oact = {None: O.ACT_NONE, "gelu_tanh": O.ACT_GELU_TANH, "gelu": O.ACT_GELU_ERF}[act]
         y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, bias=None if bias is None else np2t(bias, dev),
-                                     act=act, kernel=GEMV)
+                                     act=act, kernel=GEMV_TC)
         ref = O.quantized_matmul(x, wq, s, b, gs, bits, bias=bias, act=oact)
         if act:
             tol = dict(ulps=4, rl2=6e-3)
     torch.cuda.synchronize()
     assert qlinear.device_error() == 0
     assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), what=f"gemv-tc {bits} {gs} {M}x{N}x{K} {epi}", **tol)
+
+
+def test_gemv_tc_rejects_what_it_cannot_run(dev):
+    """Forcing the tcgen05 GEMV on a shape it does not take is an error, not a silent
+    fallback (Q4 with group size 32, K not a whole number of stages, M > 8)."""
+    for (M, K, gs, bits) in [(1, 1024, 32, 4), (1, 384, 64, 4), (9, 1024, 64, 4)]:
+        _, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, 128, K, gs, bits, 5)
+        with pytest.raises(qlinear.QlError):
+            qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, kernel=GEMV_TC)
+
+
+@pytest.mark.parametrize("bits,gs", [(4, 64), (4, 128), (8, 32), (8, 64), (8, 128)])
+@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("K", [1024, 2048])
+def test_gemv_tc_parity(dev, bits, gs, M, K):
+    """The tcgen05 GEMV forced on small shapes (the automatic choice sends these to the
+    mma.sync kernel): every group size and bit width it takes, M = 1..8."""
+    N = 200
+    _, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 7 * M + gs + bits)
+    y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, kernel=GEMV_TC)
+    torch.cuda.synchronize()
+    assert qlinear.device_error() == 0
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(O.quantized_matmul(x, wq, s, b, gs, bits)), what="gemv-tc")
