@@ -58,6 +58,7 @@ constexpr int BT = 256;        // tokens per tile (MMA N)
 constexpr int BW = 128;        // weight rows per CTA per tile (MMA M per CTA)
 constexpr int BK = 64;         // K per pipeline step (one 128-byte swizzle row of bf16)
 constexpr int AST = 4;         // TMEM A ring depth (32 columns each)
+constexpr int KR = 8;          // k-step completion ring (>= STAGES and AST)
 constexpr int NTHREADS = 512;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t ACC_COL = 0;
@@ -80,7 +81,8 @@ struct Cfg {
     static constexpr int SMEM_XCH = SMEM_W + STAGES * W_STAGE_BYTES;  // swiglu exchange
     static constexpr int XCH_BYTES = 64 * 33 * 4;
     static constexpr int SMEM_BAR = SMEM_XCH + XCH_BYTES;
-    static constexpr int NBAR = 3 * STAGES + 2 * AST + 2;
+    static constexpr int NBAR = 3 * STAGES + AST + KR + 2;
+    static_assert(KR >= STAGES && KR >= AST, "k-step ring");
     static constexpr int SMEM_MISC = SMEM_BAR + NBAR * 8;
     static constexpr int SMEM_TOTAL = SMEM_MISC + 16 + 1024;  // + alignment slack
 };
@@ -127,10 +129,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::SMEM_BAR);
     uint64_t *xfull = bars;                 // x halves landed (used in the leader CTA)
     uint64_t *wfull = bars + STAGES;        // packed W landed (local)
-    uint64_t *empty = bars + 2 * STAGES;    // stage free: MMA done + local dequant done
+    uint64_t *empty = bars + 2 * STAGES;    // packed W of the stage read by the local dequant warps
     uint64_t *afull = bars + 3 * STAGES;    // TMEM A slot written (leader: both CTAs' warps)
-    uint64_t *aempty = afull + AST;         // TMEM A slot consumed by the MMA
-    uint64_t *accfull = aempty + AST;       // accumulator complete
+    // MMAs of k-step i complete (one commit per step: a commit stalls the issuing thread
+    // until the tensor pipe drains).  It frees the x stage (producer, step i + STAGES) and
+    // the TMEM A slot (dequant, step i + AST).
+    uint64_t *kdone = afull + AST;
+    uint64_t *accfull = kdone + KR;         // accumulator complete
     uint64_t *accempty = accfull + 1;       // accumulator drained (leader: both CTAs' warps)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::SMEM_MISC);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::SMEM_MISC + 4);
@@ -150,12 +155,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&xfull[s], 1);
             mbar_init(&wfull[s], 1);
-            mbar_init(&empty[s], 1 + 4);  // MMA commit + 4 local dequant warps
+            mbar_init(&empty[s], 4);  // 4 local dequant warps
         }
-        for (int j = 0; j < AST; ++j) {
-            mbar_init(&afull[j], 4 * CG);
-            mbar_init(&aempty[j], 1);
-        }
+        for (int j = 0; j < AST; ++j) mbar_init(&afull[j], 4 * CG);
+        for (int j = 0; j < KR; ++j) mbar_init(&kdone[j], 1);
         mbar_init(accfull, 1);
         mbar_init(accempty, 4 * CG);
         *abort_flag = 0;
@@ -190,6 +193,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     if (!TR_WAIT(0, mbar_wait<CG == 2>(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY,
                                    peer_abort)))
                         break;
+                    if (it >= (uint32_t)STAGES) {  // the MMAs that read this x stage are done
+                        const uint32_t i = it - STAGES;
+                        if (!TR_WAIT(0, mbar_wait<CG == 2>(&kdone[i % KR], (i / KR) & 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY,
+                                                           peer_abort)))
+                            break;
+                    }
                     uint8_t *xs = smem + C::SMEM_X + s * C::X_STAGE_BYTES;
                     uint8_t *ws = smem + C::SMEM_W + s * C::W_STAGE_BYTES;
                     const bool wstep = kt < p.ktw;
@@ -251,13 +260,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                       (kt | kk) != 0);
                     }
                     if (CG == 2) {  // signal both CTAs of the pair
-                        tc_commit_pair(smem_u32(&empty[s]));
-                        tc_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));
-                        tc_commit_pair(smem_u32(&aempty[j]));
-                        tc_commit_pair(mapa_shared(smem_u32(&aempty[j]), 1));
+                        tc_commit_pair(smem_u32(&kdone[it % KR]));
+                        tc_commit_pair(mapa_shared(smem_u32(&kdone[it % KR]), 1));
                     } else {
-                        tc_commit(&empty[s]);
-                        tc_commit(&aempty[j]);
+                        tc_commit(&kdone[it % KR]);
                     }
                 }
                 if (!ok) break;
@@ -416,7 +422,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int lt = (int)(it / (uint32_t)KT), kt = (int)(it - (uint32_t)lt * KT);
             const int s = it % STAGES, j = it % AST;
             if (!TR_WAIT(warp == 8 ? 5 : 15, mbar_wait<CG == 2>(&wfull[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort)) ||
-                !TR_WAIT(warp == 8 ? 6 : 15, mbar_wait<CG == 2>(&aempty[j], ((it / AST) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY, peer_abort)))
+                (it >= (uint32_t)AST &&  // the MMAs of step it - AST released this A slot
+                 !TR_WAIT(warp == 8 ? 6 : 15, mbar_wait<CG == 2>(&kdone[(it - AST) % KR], ((it - AST) / KR) & 1, abort_flag,
+                                                                 DEV_ERR_TIMEOUT_EMPTY, peer_abort))))
                 break;
             uint32_t r[32];
 #ifdef QL_EXP_NODQ
