@@ -21,7 +21,9 @@ Also reported (rank 0, N = 1):
     D2H of the block output inside the timed region);
   * "cpu_baseline": the CPU oracle (oracle/qref.c, fast mode, all host threads) on a
     bounded sample of the workload;
-  * "decode_gemv": the Llama-3.2-3B Q4 decode step at M = 1 in HBM GB/s.
+  * "decode_gemv": the Llama-3.2-3B Q4 decode step at M = 1 in HBM GB/s,
+    with the lm_head alone and the step at M = 4 and 8;
+  * "other_configs": cfg1, the Z-Image block with LoRA and the Wan block at full size.
 
 `--impl reference` times the reference path's CPU implementation instead (the oracle
 restatement of MLX's affine quantized_matmul; MLX itself cannot be built here).
@@ -176,8 +178,9 @@ def cpu_baseline_sample(cfg):
             "sample": f"{Ms} of {cfg['M']} tokens through the 4 FLUX block linears (oracle fast mode)"}
 
 
-def decode_gemv(dev, steps=20, warmup=5):
-    """Llama-3.2-3B Q4 g64 decode step at M=1: 28 x (qkv, o, gate/up SwiGLU, down) + lm_head."""
+def decode_gemv(dev, steps=20, warmup=5, M=1, head=True):
+    """Llama-3.2-3B Q4 g64 decode step at M tokens: 28 x (qkv, o, gate/up SwiGLU, down) +
+    lm_head; `head` also times the lm_head alone."""
     import torch
     import qlinear
 
@@ -192,12 +195,12 @@ def decode_gemv(dev, steps=20, warmup=5):
     for _ in range(L):
         layers.append(dict(qkv=qlin(H + 2 * KV, H), o=qlin(H, H), gate=qlin(I, H), up=qlin(I, H), down=qlin(H, I)))
     head = qlin(V, H)
-    h = torch.randn(1, H, device=dev, generator=g).to(torch.bfloat16)
-    bufs = dict(qkv=torch.empty(1, H + 2 * KV, device=dev, dtype=torch.bfloat16),
-                o=torch.empty(1, H, device=dev, dtype=torch.bfloat16),
-                g=torch.empty(1, I, device=dev, dtype=torch.bfloat16),
-                h=torch.empty(1, H, device=dev, dtype=torch.bfloat16),
-                logits=torch.empty(1, V, device=dev, dtype=torch.bfloat16))
+    h = torch.randn(M, H, device=dev, generator=g).to(torch.bfloat16)
+    bufs = dict(qkv=torch.empty(M, H + 2 * KV, device=dev, dtype=torch.bfloat16),
+                o=torch.empty(M, H, device=dev, dtype=torch.bfloat16),
+                g=torch.empty(M, I, device=dev, dtype=torch.bfloat16),
+                h=torch.empty(M, H, device=dev, dtype=torch.bfloat16),
+                logits=torch.empty(M, V, device=dev, dtype=torch.bfloat16))
 
     def step():
         x = h
@@ -210,7 +213,7 @@ def decode_gemv(dev, steps=20, warmup=5):
         qlinear.quantized_matmul(x, *head, True, 64, 4, out=bufs["logits"])
 
     def nbytes(N, K):
-        return N * K * 4 // 8 + N * (K // 64) * 4 + (K + N) * 2
+        return N * K * 4 // 8 + N * (K // 64) * 4 + M * (K + N) * 2
 
     per_layer = nbytes(H + 2 * KV, H) + nbytes(H, H) + 2 * nbytes(I, H) - (H * 2) + nbytes(H, I)
     total_bytes = L * per_layer + nbytes(V, H)
@@ -235,6 +238,11 @@ def decode_gemv(dev, steps=20, warmup=5):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
+    res = {"workload": f"llama3.2-3b_q4_g64_decode_M{M}", "value": total_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
+           "ms_per_step": ms, "bytes_per_step": total_bytes, "launches_per_step": 4 * L + 1,
+           "timing": "CUDA graph of one decode step; 1.8 GB of weights per step (> L2)"}
+    if not head:
+        return res
     # the lm_head alone (one 197 MB GEMV, the largest single launch of the step)
     def head_only():
         for _ in range(4):
@@ -257,11 +265,91 @@ def decode_gemv(dev, steps=20, warmup=5):
     e1.record()
     torch.cuda.synchronize()
     head_ms = e0.elapsed_time(e1) / 20
-    return {"workload": "llama3.2-3b_q4_g64_decode_M1", "value": total_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
-            "ms_per_step": ms, "bytes_per_step": total_bytes, "launches_per_step": 4 * L + 1,
-            "timing": "CUDA graph of one decode step; 1.8 GB of weights per step (> L2)",
-            "lm_head_gemv": {"value": nbytes(V, H) / (head_ms * 1e-3) / 1e9, "unit": "GB/s", "us": head_ms * 1e3,
-                             "shape": "M=1 N=128256 K=3072 Q4 g64 (197 MB > L2), 20 launches in a graph"}}
+    res["lm_head_gemv"] = {"value": nbytes(V, H) / (head_ms * 1e-3) / 1e9, "unit": "GB/s", "us": head_ms * 1e3,
+                           "shape": f"M={M} N=128256 K=3072 Q4 g64 (197 MB > L2), 20 launches in a graph"}
+    return res
+
+
+def other_configs(dev, iters=5):
+    """The other BASELINE configs' GEMM shapes at full size (TFLOP/s, 2*M*N*K per linear,
+    LoRA flops not counted): cfg1 (M=4096, 3072x3072 Q4), Z-Image block (M=4608 Q4,
+    4 x 3840^2 attention linears and the MLP down with LoRA r=32 fused, the SwiGLU pair
+    fused), Wan block (M=32760 Q4, 6 x 5120^2, 5120->13824 + GELU, 13824->5120)."""
+    import torch
+    import qlinear
+
+    g = torch.Generator(device=dev).manual_seed(5)
+
+    def qlin(N, K, bits, gs=64):
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        return qlinear.quantize(w, gs, bits)
+
+    def lora(N, K, r=32):
+        a = (torch.randn(K, r, device=dev, generator=g) / r ** 0.5).to(torch.bfloat16)
+        b = (torch.randn(r, N, device=dev, generator=g) * 0.01).to(torch.bfloat16)
+        return (a, b, 1.0)
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
+
+    out = {}
+    # cfg1
+    M = 4096
+    w1 = qlin(3072, 3072, 4)
+    x = torch.randn(M, 3072, device=dev, generator=g).to(torch.bfloat16)
+    y = torch.empty(M, 3072, device=dev, dtype=torch.bfloat16)
+    ms = timed(lambda: qlinear.quantized_matmul(x, *w1, True, 64, 4, out=y))
+    fl = 2 * M * 3072 * 3072
+    out["cfg1_q4_4096x3072x3072"] = {"value": fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms}
+    del w1, x, y
+    # Z-Image block (Q4, LoRA r=32 on the attention linears and the MLP down)
+    M, D, F = 4608, 3840, 10240
+    att = [(qlin(D, D, 4), lora(D, D)) for _ in range(4)]
+    w1, w3 = qlin(F, D, 4), qlin(F, D, 4)
+    w2, l2 = qlin(D, F, 4), lora(D, F)
+    x = torch.randn(M, D, device=dev, generator=g).to(torch.bfloat16)
+    ya = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
+    yf = torch.empty(M, F, device=dev, dtype=torch.bfloat16)
+    ws = torch.empty(qlinear.workspace_size(M, F, F, 32), dtype=torch.uint8, device=dev)
+
+    def zimage():
+        for wq, lo in att:
+            qlinear.quantized_matmul(x, *wq, True, 64, 4, lora=lo, workspace=ws, out=ya)
+        qlinear.quantized_matmul(x, *w1, True, 64, 4, act="swiglu", up=w3, out=yf)
+        qlinear.quantized_matmul(yf, *w2, True, 64, 4, lora=l2, workspace=ws, out=ya)
+
+    ms = timed(zimage)
+    fl = 2 * M * (4 * D * D + 2 * F * D + D * F)
+    out["zimage_q4_lora32_block"] = {"value": fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms,
+                                     "lora_gflop_not_counted": 2 * M * 32 * (5 * D + 4 * D + F) / 1e9}
+    del att, w1, w3, w2, x, ya, yf, ws
+    # Wan block (Q4, M=32760)
+    M, D, F = 32760, 5120, 13824
+    sq = [qlin(D, D, 4) for _ in range(6)]
+    up, dn = qlin(F, D, 4), qlin(D, F, 4)
+    x = torch.randn(M, D, device=dev, generator=g).to(torch.bfloat16)
+    ya = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
+    yf = torch.empty(M, F, device=dev, dtype=torch.bfloat16)
+
+    def wan():
+        for wq in sq:
+            qlinear.quantized_matmul(x, *wq, True, 64, 4, out=ya)
+        qlinear.quantized_matmul(x, *up, True, 64, 4, act="gelu_tanh", out=yf)
+        qlinear.quantized_matmul(yf, *dn, True, 64, 4, out=ya)
+
+    ms = timed(wan)
+    fl = 2 * M * (6 * D * D + 2 * F * D)
+    out["wan_q4_block"] = {"value": fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms}
+    return out
 
 
 def run_ours(args):
@@ -433,6 +521,11 @@ def run_ours(args):
             result["decode_gemv"]["frac_of_hbm"] = result["decode_gemv"]["value"] / peaks["hbm_gbs"]
             lm = result["decode_gemv"]["lm_head_gemv"]
             lm["frac_of_hbm"] = lm["value"] / peaks["hbm_gbs"]
+            for m in (4, 8):
+                d = decode_gemv(dev, M=m, head=False)
+                result["decode_gemv"][f"M{m}"] = {"value": d["value"], "unit": "GB/s", "ms_per_step": d["ms_per_step"],
+                                                  "frac_of_hbm": d["value"] / peaks["hbm_gbs"]}
+            result["other_configs"] = other_configs(dev)
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.destroy_process_group()

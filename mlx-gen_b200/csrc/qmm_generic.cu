@@ -110,45 +110,163 @@ __global__ void __launch_bounds__(256) qmm_generic_kernel(const Params p) {
         }
 }
 
-// T[m, j] = bf16(scale * sum_k x[m,k] A[k,j]) for j < rank, 0 for rank <= j < rpad.
-// One CTA per 32 rows of x; x and A chunks are staged through shared memory.
-__global__ void __launch_bounds__(256) lora_t_kernel(const __nv_bfloat16 *__restrict__ x, int M, int K,
-                                                     const __nv_bfloat16 *__restrict__ A, int rank, int rpad,
-                                                     float scale, __nv_bfloat16 *__restrict__ T) {
-    constexpr int R = 32, KC = 64;
-    __shared__ float xs[R][KC + 1];
-    __shared__ float as[KC][64 + 1];
-    const int m0 = blockIdx.x * R;
-    for (int jb = 0; jb < rpad; jb += 64) {
-        // each thread: row r = tid / 8, columns jb + (tid % 8) + 8*c, c < 8
-        const int r = threadIdx.x >> 3, cj = threadIdx.x & 7;
-        float acc[8] = {};
-        for (int k0 = 0; k0 < K; k0 += KC) {
-            for (int i = threadIdx.x; i < R * KC; i += 256) {
-                const int rr = i / KC, kk = i % KC, m = m0 + rr, k = k0 + kk;
-                xs[rr][kk] = (m < M && k < K) ? __bfloat162float(x[(int64_t)m * K + k]) : 0.f;
-            }
-            for (int i = threadIdx.x; i < KC * 64; i += 256) {
-                const int kk = i / 64, jj = i % 64, k = k0 + kk, j = jb + jj;
-                as[kk][jj] = (k < K && j < rank) ? __bfloat162float(A[(int64_t)k * rank + j]) : 0.f;
-            }
-            __syncthreads();
-            for (int kk = 0; kk < KC; ++kk) {
-                const float xv = xs[r][kk];
-#pragma unroll
-                for (int c = 0; c < 8; ++c) acc[c] += xv * as[kk][cj + 8 * c];
-            }
-            __syncthreads();
+// LoRA pre-pass on tensor cores: T[M, rpad] = bf16(scale * (x . A)), columns >= rank zero.
+// x [M, K] bf16 (read once, the cost of this pass), A [K, rank] bf16 (small, L2-resident).
+// CTA tile 32 rows x 64 columns of T, 4 warps of 16 x 32; K in chunks of 64 through a
+// 8-deep cp.async ring of 128-byte rows with a 16-byte-unit XOR swizzle (conflict-free
+// ldmatrix); mma.sync.m16n8k16 bf16 with fp32 accumulation.
+namespace lt {
+constexpr int BM = 32, BN = 64, BKC = 64, ST = 8;
+constexpr int SMEM = ST * (BM + BKC) * 128 + 1024;
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t r[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t r[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// byte offset of 16-byte unit c of 128-byte row r
+__device__ __forceinline__ int swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+// TMA: thread 0 loads each chunk with two tensor-map boxes (x: 64 K x 32 rows, A: 64
+// columns x 64 K, both 128-byte swizzled, which is the layout swz() reads); otherwise
+// every thread issues 16-byte cp.async copies (A's rank not a multiple of 8).
+template <bool TMA>
+__global__ void __launch_bounds__(128) lora_t_mma_kernel(const __grid_constant__ CUtensorMap tm_x,
+                                                          const __grid_constant__ CUtensorMap tm_a,
+                                                          const __nv_bfloat16 *__restrict__ x, int M, int K,
+                                                          const __nv_bfloat16 *__restrict__ A, int rank, int rpad,
+                                                          float scale, __nv_bfloat16 *__restrict__ T, int vec_a) {
+    extern __shared__ uint8_t lt_smem_raw[];
+    __shared__ uint64_t full[ST];
+    __shared__ int abort_flag;
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(lt_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t(*sx)[BM * 128] = reinterpret_cast<uint8_t(*)[BM * 128]>(base);
+    uint8_t(*sa)[BKC * 128] = reinterpret_cast<uint8_t(*)[BKC * 128]>(base + ST * BM * 128);
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wm = warp & 1, wn = warp >> 1;  // rows 16 wm .. +16, columns 32 wn .. +32 of the tile
+    const int nk = (K + BKC - 1) / BKC;
+
+    // CTAs start at different K chunks so that they do not all read the same lines of A
+    // at once (144 CTAs on one L2 line serialise); each CTA still sums its chunks in order
+    const int kstart = (int)((blockIdx.x * 5u) % (unsigned)nk);
+    if (TMA) {
+        if (tid == 0) {
+            for (int i = 0; i < ST; ++i) mbar_init(&full[i], 1);
+            abort_flag = 0;
+            mbar_fence_init();
         }
-        const int m = m0 + r;
-        if (m < M)
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const int j = jb + cj + 8 * c;
-                T[(int64_t)m * rpad + j] = __float2bfloat16_rn(j < rank ? scale * acc[c] : 0.f);
+        __syncthreads();
+    }
+    auto load = [&](int kc, int s) {
+        int kr = kc + kstart;
+        if (kr >= nk) kr -= nk;
+        const int k0 = kr * BKC;
+        if (TMA) {
+            if (tid == 0) {
+                mbar_arrive_expect_tx(&full[s], (BM + BKC) * 128);
+                tma_load_2d(sx[s], &tm_x, &full[s], k0, m0);
+                tma_load_2d(sa[s], &tm_a, &full[s], n0, k0);
             }
+            return;
+        }
+        for (int i = tid; i < BM * 8; i += 128) {
+            const int r = i >> 3, c = i & 7, m = m0 + r, k = k0 + c * 8;
+            const bool ok = m < M && k < K;  // K is a multiple of 8
+            cp_async16(sx[s] + swz(r, c), ok ? (const void *)(x + (int64_t)m * K + k) : (const void *)x, ok ? 16 : 0);
+        }
+        for (int i = tid; i < BKC * 8; i += 128) {
+            const int r = i >> 3, c = i & 7, k = k0 + r, n = n0 + c * 8;
+            if (vec_a) {
+                const bool ok = k < K && n < rank;  // rank is a multiple of 8 here
+                cp_async16(sa[s] + swz(r, c), ok ? (const void *)(A + (int64_t)k * rank + n) : (const void *)A,
+                           ok ? 16 : 0);
+            } else {
+                uint16_t v[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    v[e] = (k < K && n + e < rank) ? reinterpret_cast<const uint16_t *>(A)[(int64_t)k * rank + n + e] : 0;
+                *reinterpret_cast<uint4 *>(sa[s] + swz(r, c)) =
+                    make_uint4(v[0] | (uint32_t)v[1] << 16, v[2] | (uint32_t)v[3] << 16, v[4] | (uint32_t)v[5] << 16,
+                               v[6] | (uint32_t)v[7] << 16);
+            }
+        }
+    };
+
+    float acc[4][4] = {};
+#pragma unroll
+    for (int s = 0; s < ST - 1; ++s) {
+        if (s < nk) load(s, s);
+        cp_async_commit();
+    }
+    for (int kc = 0; kc < nk; ++kc) {
+        if (TMA)  // a timed-out wait only records the error: every thread keeps to the same barriers
+            mbar_wait(&full[kc % ST], (kc / ST) & 1, &abort_flag, DEV_ERR_TIMEOUT_FULL);
+        else
+            cp_async_wait<ST - 2>();
+        __syncthreads();  // chunk kc landed for every thread; stage (kc - 1) % ST is free
+#ifndef QL_EXP_LT_NOLOAD
+        if (kc + ST - 1 < nk) load(kc + ST - 1, (kc + ST - 1) % ST);
+#endif
+        cp_async_commit();
+        const int s = kc % ST;
+        const uint32_t xb = smem_u32(sx[s]), ab = smem_u32(sa[s]);
+#pragma unroll
+        for (int kk = 0; kk < BKC / 16; ++kk) {
+            uint32_t af[4];
+            ldsm_x4(xb + swz(16 * wm + (lane & 15), 2 * kk + (lane >> 4)), af);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t bf[4];
+                ldsm_x4_t(ab + swz(16 * kk + (lane & 15), 4 * wn + 2 * h + (lane >> 4)), bf);
+#ifndef QL_EXP_LT_NOMMA
+                mma_bf16(acc[2 * h], af, bf[0], bf[1]);
+                mma_bf16(acc[2 * h + 1], af, bf[2], bf[3]);
+#else
+                acc[2 * h][0] += __uint_as_float(af[0] ^ bf[0]);
+                acc[2 * h + 1][0] += __uint_as_float(af[1] ^ bf[2]);
+#endif
+            }
+        }
+    }
+    cp_async_wait<0>();
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int n = n0 + 32 * wn + 8 * j + 2 * t;
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+            const int m = m0 + 16 * wm + g + 8 * hr;
+            if (m < M) {
+                const float v0 = n < rank ? scale * acc[j][2 * hr] : 0.f;
+                const float v1 = n + 1 < rank ? scale * acc[j][2 * hr + 1] : 0.f;
+                *reinterpret_cast<uint32_t *>(T + (int64_t)m * rpad + n) = pack_bf16x2(v0, v1);
+            }
+        }
     }
 }
+}  // namespace lt
 
 }  // namespace generic
 
@@ -192,10 +310,31 @@ int launch_qmm_generic(const void *x, int xdt, int64_t M, int64_t K, const uint3
 int launch_lora_t(const void *x, int64_t M, int64_t K, const void *A, int64_t rank, float scale,
                   void *T, cudaStream_t st) {
     const int rpad = (int)((rank + 63) / 64 * 64);
-    const int grid = (int)((M + 31) / 32);
-    generic::lora_t_kernel<<<grid, 256, 0, st>>>((const __nv_bfloat16 *)x, (int)M, (int)K,
-                                                  (const __nv_bfloat16 *)A, (int)rank, rpad, scale,
-                                                  (__nv_bfloat16 *)T);
+    using namespace generic::lt;
+    const int vec_a = rank % 8 == 0 && reinterpret_cast<uintptr_t>(A) % 16 == 0;
+    const dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)(rpad / BN));
+    static bool configured = false;
+    if (!configured) {
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        configured = true;
+    }
+    CUtensorMap mx{}, ma{};
+    if (vec_a) {
+        if (int rc = gemm::make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, (uint64_t)K, (uint64_t)M,
+                                       (uint64_t)K * 2, BKC, BM, CU_TENSOR_MAP_SWIZZLE_128B))
+            return rc;
+        if (int rc = gemm::make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, (uint64_t)rank, (uint64_t)K,
+                                       (uint64_t)rank * 2, BN, BKC, CU_TENSOR_MAP_SWIZZLE_128B))
+            return rc;
+        lora_t_mma_kernel<true><<<grid, 128, SMEM, st>>>(mx, ma, (const __nv_bfloat16 *)x, (int)M, (int)K,
+                                                         (const __nv_bfloat16 *)A, (int)rank, rpad, scale,
+                                                         (__nv_bfloat16 *)T, vec_a);
+    } else {
+        lora_t_mma_kernel<false><<<grid, 128, SMEM, st>>>(mx, ma, (const __nv_bfloat16 *)x, (int)M, (int)K,
+                                                          (const __nv_bfloat16 *)A, (int)rank, rpad, scale,
+                                                          (__nv_bfloat16 *)T, vec_a);
+    }
     QL_CUDA_TRY(cudaGetLastError());
     return QL_OK;
 }
