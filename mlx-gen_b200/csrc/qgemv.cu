@@ -298,8 +298,9 @@ int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const 
     // mma.sync kernel (qgemv_tma.cu), else the register-fed one below
     static const bool force_regs = getenv("QL_GEMV_REGS") != nullptr;  // profiling switches
     static const bool force_mma = getenv("QL_GEMV_MMA") != nullptr;
-    // The tcgen05 kernel wins once its row tiles (128 rows, 64 with SwiGLU) fill the GPU;
-    // below that its fixed start-up (TMEM, activation conversion, pipeline fill) dominates.
+    // The tcgen05 kernel wins once its row tiles (128 rows, 64 with SwiGLU) fill the GPU,
+    // or at 6+ tokens (the mma.sync kernel's per-token folds grow with M); below that its
+    // fixed start-up (TMEM, activation conversion, pipeline fill) dominates.
     static int n_sms = 0;
     if (!n_sms) {
         int dev = 0;
@@ -309,7 +310,7 @@ int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const 
     }
     static const bool force_tc = getenv("QL_GEMV_TC") != nullptr;
     const int64_t tiles = (N + (act == QL_ACT_SWIGLU ? 63 : 127)) / (act == QL_ACT_SWIGLU ? 64 : 128);
-    if (!force_regs && !force_mma && (force_tc || tiles >= n_sms) &&
+    if (!force_regs && !force_mma && (force_tc || tiles >= n_sms || M >= 6) &&
         qgemv_tc_supported(M, K, gs, bits, x, lora_t != nullptr) && all_aligned16({scales, biases, scales2, biases2}))
         return launch_qgemv_tc(x, M, K, wq, scales, biases, wq2, scales2, biases2, N, gs, bits, bias, bias2, act, y,
                                st);

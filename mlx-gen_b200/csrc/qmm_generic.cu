@@ -151,7 +151,9 @@ __device__ __forceinline__ int swz(int r, int c) { return r * 128 + ((c ^ (r & 7
 // TMA: thread 0 loads each chunk with two tensor-map boxes (x: 64 K x 32 rows, A: 64
 // columns x 64 K, both 128-byte swizzled, which is the layout swz() reads); otherwise
 // every thread issues 16-byte cp.async copies (A's rank not a multiple of 8).
-template <bool TMA>
+// NH = 16-column halves per warp: 2 computes all 64 columns of the tile, 1 only the first
+// 32 (rank <= 32) and writes zeros to the rest.
+template <bool TMA, int NH>
 __global__ void __launch_bounds__(128) lora_t_mma_kernel(const __grid_constant__ CUtensorMap tm_x,
                                                           const __grid_constant__ CUtensorMap tm_a,
                                                           const __nv_bfloat16 *__restrict__ x, int M, int K,
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(128) lora_t_mma_kernel(const __grid_constant__
     uint8_t(*sa)[BKC * 128] = reinterpret_cast<uint8_t(*)[BKC * 128]>(base + ST * BM * 128);
     const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int wm = warp & 1, wn = warp >> 1;  // rows 16 wm .. +16, columns 32 wn .. +32 of the tile
+    const int wm = warp & 1, wn = warp >> 1;  // rows 16 wm .. +16, columns 16 NH wn .. + 16 NH
     const int nk = (K + BKC - 1) / BKC;
 
     // CTAs start at different K chunks so that they do not all read the same lines of A
@@ -214,7 +216,7 @@ __global__ void __launch_bounds__(128) lora_t_mma_kernel(const __grid_constant__
         }
     };
 
-    float acc[4][4] = {};
+    float acc[2 * NH][4] = {};
 #pragma unroll
     for (int s = 0; s < ST - 1; ++s) {
         if (s < nk) load(s, s);
@@ -237,9 +239,9 @@ __global__ void __launch_bounds__(128) lora_t_mma_kernel(const __grid_constant__
             uint32_t af[4];
             ldsm_x4(xb + swz(16 * wm + (lane & 15), 2 * kk + (lane >> 4)), af);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
+            for (int h = 0; h < NH; ++h) {
                 uint32_t bf[4];
-                ldsm_x4_t(ab + swz(16 * kk + (lane & 15), 4 * wn + 2 * h + (lane >> 4)), bf);
+                ldsm_x4_t(ab + swz(16 * kk + (lane & 15), 2 * NH * wn + 2 * h + (lane >> 4)), bf);
 #ifndef QL_EXP_LT_NOMMA
                 mma_bf16(acc[2 * h], af, bf[0], bf[1]);
                 mma_bf16(acc[2 * h + 1], af, bf[2], bf[3]);
@@ -253,8 +255,8 @@ __global__ void __launch_bounds__(128) lora_t_mma_kernel(const __grid_constant__
     cp_async_wait<0>();
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int n = n0 + 32 * wn + 8 * j + 2 * t;
+    for (int j = 0; j < 2 * NH; ++j) {
+        const int n = n0 + 16 * NH * wn + 8 * j + 2 * t;
 #pragma unroll
         for (int hr = 0; hr < 2; ++hr) {
             const int m = m0 + 16 * wm + g + 8 * hr;
@@ -262,6 +264,7 @@ __global__ void __launch_bounds__(128) lora_t_mma_kernel(const __grid_constant__
                 const float v0 = n < rank ? scale * acc[j][2 * hr] : 0.f;
                 const float v1 = n + 1 < rank ? scale * acc[j][2 * hr + 1] : 0.f;
                 *reinterpret_cast<uint32_t *>(T + (int64_t)m * rpad + n) = pack_bf16x2(v0, v1);
+                if (NH == 1) *reinterpret_cast<uint32_t *>(T + (int64_t)m * rpad + n + 32) = 0u;
             }
         }
     }
@@ -315,8 +318,10 @@ int launch_lora_t(const void *x, int64_t M, int64_t K, const void *A, int64_t ra
     const dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)(rpad / BN));
     static bool configured = false;
     if (!configured) {
-        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         configured = true;
     }
     CUtensorMap mx{}, ma{};
@@ -327,11 +332,13 @@ int launch_lora_t(const void *x, int64_t M, int64_t K, const void *A, int64_t ra
         if (int rc = gemm::make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, (uint64_t)rank, (uint64_t)K,
                                        (uint64_t)rank * 2, BN, BKC, CU_TENSOR_MAP_SWIZZLE_128B))
             return rc;
-        lora_t_mma_kernel<true><<<grid, 128, SMEM, st>>>(mx, ma, (const __nv_bfloat16 *)x, (int)M, (int)K,
+        auto kfn = rank <= 32 ? lora_t_mma_kernel<true, 1> : lora_t_mma_kernel<true, 2>;
+        kfn<<<grid, 128, SMEM, st>>>(mx, ma, (const __nv_bfloat16 *)x, (int)M, (int)K,
                                                          (const __nv_bfloat16 *)A, (int)rank, rpad, scale,
                                                          (__nv_bfloat16 *)T, vec_a);
     } else {
-        lora_t_mma_kernel<false><<<grid, 128, SMEM, st>>>(mx, ma, (const __nv_bfloat16 *)x, (int)M, (int)K,
+        auto kfn = rank <= 32 ? lora_t_mma_kernel<false, 1> : lora_t_mma_kernel<false, 2>;
+        kfn<<<grid, 128, SMEM, st>>>(mx, ma, (const __nv_bfloat16 *)x, (int)M, (int)K,
                                                           (const __nv_bfloat16 *)A, (int)rank, rpad, scale,
                                                           (__nv_bfloat16 *)T, vec_a);
     }

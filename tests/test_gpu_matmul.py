@@ -90,7 +90,7 @@ def test_swiglu_epilogue(dev, kernel, bits):
 
 
 @pytest.mark.parametrize("kernel", [GEMV, GEMM, GEMM2, GENERIC])
-@pytest.mark.parametrize("rank", [8, 32, 96])
+@pytest.mark.parametrize("rank", [8, 12, 32, 96])
 def test_lora_epilogue(dev, kernel, rank):
     """LoRA residual scale*(x.A).B fused into the accumulator (src/adapters.rs:260-270).  The
     reference rounds the base output and the residual to bf16 separately before summing them;
