@@ -11,8 +11,9 @@ activations ~N(0, 1), seeded synthetic data (no checkpoint or dataset involved).
 Each step touches ~300 MB (> the 126 MB L2), so no explicit L2 flush is needed.
 
 N > 1 GPUs (torchrun, one rank per GPU, NCCL): Megatron tensor parallelism of the same
-block -- QKV / up column-parallel, out / down row-parallel with one all-reduce each --
-so total work is fixed ("scaling": "strong").
+block -- QKV / up column-parallel, out / down row-parallel with one all-reduce each, run
+in M-slices so a slice's all-reduce overlaps the next slice's GEMM, every linear waiting
+for the reduced output it reads -- so total work is fixed ("scaling": "strong").
 
 Also reported (rank 0, N = 1):
   * "roofline": the tcgen05 GEMM kernel's achieved TFLOP/s (algorithmic 2*M*N*K per
@@ -23,7 +24,9 @@ Also reported (rank 0, N = 1):
     bounded sample of the workload;
   * "decode_gemv": the Llama-3.2-3B Q4 decode step at M = 1 in HBM GB/s,
     with the lm_head alone and the step at M = 4 and 8;
-  * "other_configs": cfg1, the Z-Image block with LoRA and the Wan block at full size.
+  * "other_configs": cfg1 and the Z-Image block with LoRA at full size;
+  * "wan_block": the Wan2.2-shaped block (configs[4], M = 32760 Q4), the multi-GPU scaling
+    workload, timed with the same tensor parallelism at every N.
 
 `--impl reference` times the reference path's CPU implementation instead (the oracle
 restatement of MLX's affine quantized_matmul; MLX itself cannot be built here).
@@ -46,15 +49,35 @@ FLUX = dict(M=4608, hidden=3072, mlp=12288, bits=8, gs=64)
 METRIC = "quantized_matmul TFLOP/s (DiT M) and HBM GB/s (M=1) vs B200 peak"
 
 
+WAN = dict(M=32760, hidden=5120, mlp=13824, bits=4, gs=64)
+
+
 def flux_linears(cfg):
+    """(name, N, K, act, tensor-parallel style, input).  The input is "x" (the block input),
+    "attn" (a stand-in for the attention output, which is not part of this path) or the
+    name of an earlier linear: each linear waits for the one it reads, all-reduce
+    included, as in a real forward pass."""
     h, f = cfg["hidden"], cfg["mlp"]
-    # name, N, K, act, parallel style
-    return [("qkv", 3 * h, h, None, "col"), ("out", h, h, None, "row"),
-            ("up", f, h, "gelu_tanh", "col"), ("down", h, f, None, "row")]
+    return [("qkv", 3 * h, h, None, "col", "x"), ("out", h, h, None, "row", "attn"),
+            ("up", f, h, "gelu_tanh", "col", "out"), ("down", h, f, None, "row", "up")]
+
+
+def wan_linears(cfg):
+    """Wan2.2 block linears: self-attention q, k, v, o, cross-attention q, o (its k, v act
+    on the 512 text tokens and are left out), FFN up (+GELU-tanh) and down: three
+    row-parallel linears, so three all-reduces per block under TP."""
+    h, f = cfg["hidden"], cfg["mlp"]
+    return [("q", h, h, None, "col", "x"), ("k", h, h, None, "col", "x"), ("v", h, h, None, "col", "x"),
+            ("o", h, h, None, "row", "v"), ("cq", h, h, None, "col", "o"), ("co", h, h, None, "row", "cq"),
+            ("up", f, h, "gelu_tanh", "col", "co"), ("down", h, f, None, "row", "up")]
+
+
+def block_flops(cfg, linears):
+    return sum(2.0 * cfg["M"] * N * K for _, N, K, _, _, _ in linears(cfg))
 
 
 def flux_flops(cfg):
-    return sum(2.0 * cfg["M"] * N * K for _, N, K, _, _ in flux_linears(cfg))
+    return block_flops(cfg, flux_linears)
 
 
 def load_peaks():
@@ -274,7 +297,7 @@ def other_configs(dev, iters=5):
     """The other BASELINE configs' GEMM shapes at full size (TFLOP/s, 2*M*N*K per linear,
     LoRA flops not counted): cfg1 (M=4096, 3072x3072 Q4), Z-Image block (M=4608 Q4,
     4 x 3840^2 attention linears and the MLP down with LoRA r=32 fused, the SwiGLU pair
-    fused), Wan block (M=32760 Q4, 6 x 5120^2, 5120->13824 + GELU, 13824->5120)."""
+    fused).  The Wan block is timed at every N by run_ours ("wan_block")."""
     import torch
     import qlinear
 
@@ -331,25 +354,111 @@ def other_configs(dev, iters=5):
     fl = 2 * M * (4 * D * D + 2 * F * D + D * F)
     out["zimage_q4_lora32_block"] = {"value": fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms,
                                      "lora_gflop_not_counted": 2 * M * 32 * (5 * D + 4 * D + F) / 1e9}
-    del att, w1, w3, w2, x, ya, yf, ws
-    # Wan block (Q4, M=32760)
-    M, D, F = 32760, 5120, 13824
-    sq = [qlin(D, D, 4) for _ in range(6)]
-    up, dn = qlin(F, D, 4), qlin(D, F, 4)
-    x = torch.randn(M, D, device=dev, generator=g).to(torch.bfloat16)
-    ya = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
-    yf = torch.empty(M, F, device=dev, dtype=torch.bfloat16)
-
-    def wan():
-        for wq in sq:
-            qlinear.quantized_matmul(x, *wq, True, 64, 4, out=ya)
-        qlinear.quantized_matmul(x, *up, True, 64, 4, act="gelu_tanh", out=yf)
-        qlinear.quantized_matmul(yf, *dn, True, 64, 4, out=ya)
-
-    ms = timed(wan)
-    fl = 2 * M * (6 * D * D + 2 * F * D)
-    out["wan_q4_block"] = {"value": fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms}
     return out
+
+
+class TPBlock:
+    """The linears of one DiT block, Megatron-sharded over the ranks (N = 1: unsharded).
+
+    Column-parallel linears hold N/world packed rows; row-parallel ones hold K/world
+    (group-aligned) and are followed by an NCCL all-reduce of their output.  A row-parallel
+    linear runs in `chunks` slices of M: the all-reduce of slice i (second stream) overlaps
+    the GEMM of slice i + 1, and the next linear starts only after the last reduction -- the
+    data dependency of a real forward pass.  The GEMMs leave `comm_sms` SMs to NCCL."""
+
+    def __init__(self, cfg, linears, dev, seed, rank, world, comm_sms, chunks):
+        import torch
+        import qlinear
+        from qlinear import tp
+
+        self.cfg, self.world, self.dev = cfg, world, dev
+        self.M, self.gs, self.bits = cfg["M"], cfg["gs"], cfg["bits"]
+        self.spec = linears(cfg)
+        self.chunks = chunks if world > 1 else 1
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.lin = {}
+        for name, N, K, act, style, src in self.spec:
+            w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            bias = (torch.randn(N, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            wq, sc, bi = qlinear.quantize(w, self.gs, self.bits)
+            del w
+            if world > 1 and style == "col":
+                wq, sc, bi, bias = tp.column_shard(wq, sc, bi, bias, rank, world)
+            elif world > 1 and style == "row":
+                wq, sc, bi, _, _ = tp.row_shard(wq, sc, bi, self.gs, self.bits, rank, world)
+                if rank != 0:
+                    bias = None  # added once: the all-reduce sums rank 0's biased partial
+            self.lin[name] = dict(wq=wq, s=sc, b=bi, bias=bias, act=act, style=style, src=src,
+                                  N=sc.shape[0], K=sc.shape[1] * self.gs)
+        self.x = torch.randn(self.M, cfg["hidden"], device=dev, generator=g).to(torch.bfloat16)
+        attn_k = next(l["K"] for l in self.lin.values() if l["src"] == "attn") if any(
+            l["src"] == "attn" for l in self.lin.values()) else 0
+        self.attn = torch.randn(self.M, attn_k, device=dev, generator=g).to(torch.bfloat16) if attn_k else None
+        self.out = {n: torch.empty(self.M, l["N"], device=dev, dtype=torch.bfloat16) for n, l in self.lin.items()}
+        self.main = torch.cuda.current_stream(dev)
+        self.comm = torch.cuda.Stream(dev) if world > 1 else None
+        self.max_ctas = 0
+        if world > 1:
+            self.max_ctas = torch.cuda.get_device_properties(dev).multi_processor_count - comm_sms
+        self.flops = block_flops(cfg, linears)
+        self.launches = sum(self.chunks if l["style"] == "row" else 1 for l in self.lin.values())
+        torch.cuda.synchronize()
+
+    def step(self, xin=None, evs=None):
+        import torch
+        import torch.distributed as dist
+        import qlinear
+
+        xin = self.x if xin is None else xin
+        for name, _, _, _, _, src in self.spec:
+            l = self.lin[name]
+            inp = xin if src == "x" else (self.attn if src == "attn" else self.out[src])
+            y = self.out[name]
+            row = self.world > 1 and l["style"] == "row"
+            n = self.chunks if row else 1
+            step_m = (self.M + n - 1) // n
+            for c in range(n):
+                r0, r1 = c * step_m, min(self.M, (c + 1) * step_m)
+                if evs is not None:
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                qlinear.quantized_matmul(inp[r0:r1], l["wq"], l["s"], l["b"], True, self.gs, self.bits,
+                                         bias=l["bias"], act=l["act"], kernel=qlinear.KERNEL_GEMM,
+                                         out=y[r0:r1], max_ctas=self.max_ctas)
+                if evs is not None:
+                    e1.record()
+                    evs.append((name, e0, e1))
+                if row:
+                    self.comm.wait_stream(self.main)
+                    with torch.cuda.stream(self.comm):
+                        dist.all_reduce(y[r0:r1])
+            if row:
+                self.main.wait_stream(self.comm)  # the consumer reads the reduced output
+        return self.out[self.spec[-1][0]]
+
+
+def time_block(blk, steps, warmup, world):
+    """Device time per step of `blk` (CUDA events, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    for _ in range(warmup):
+        blk.step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        blk.step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    if world > 1:
+        tt = torch.tensor([ms], device=blk.dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    return ms
 
 
 def run_ours(args):
@@ -365,63 +474,19 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
+        # NCCL's log (e.g. its version banner) goes to stderr: stdout carries only the JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", device_id=dev)
     cfg = dict(FLUX)
     M, gs, bits = cfg["M"], cfg["gs"], cfg["bits"]
 
     # weights: generated and quantized identically on every rank, then sharded
-    g = torch.Generator(device=dev).manual_seed(0)
-    lin = {}
-    for name, N, K, act, style in flux_linears(cfg):
-        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-        bias = (torch.randn(N, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-        wq, s, b = qlinear.quantize(w, gs, bits)
-        del w
-        if world > 1 and style == "col":
-            wq, s, b, bias = tp.column_shard(wq, s, b, bias, rank, world)
-        elif world > 1 and style == "row":
-            wq, s, b, _, _ = tp.row_shard(wq, s, b, gs, bits, rank, world)
-            if rank != 0:
-                bias = None  # added once: the all-reduce sums rank 0's biased partial
-        lin[name] = dict(wq=wq, s=s, b=b, bias=bias, act=act, style=style, N=s.shape[0], K=s.shape[1] * gs)
-    x = torch.randn(M, cfg["hidden"], device=dev, generator=g).to(torch.bfloat16)
-    out = {n: torch.empty(M, l["N"], device=dev, dtype=torch.bfloat16) for n, l in lin.items()}
-    torch.cuda.synchronize()
-
-    evs = []  # (name, start, end) of every GEMM launch in the timed region
-    # N > 1: each row-parallel output is all-reduced on a second stream so the collective
-    # overlaps the next GEMM (the out-projection's with MLP-up, MLP-down's with the next
-    # step's QKV); the GEMMs then leave `comm_sms` SMs free for the NCCL kernels.
-    main = torch.cuda.current_stream(dev)
-    comm = torch.cuda.Stream(dev) if world > 1 else None
-    ar_done = {n: torch.cuda.Event() for n in lin}
-    max_ctas = 0
-    if world > 1:
-        max_ctas = torch.cuda.get_device_properties(dev).multi_processor_count - args.comm_sms
+    blk = TPBlock(cfg, flux_linears, dev, 0, rank, world, args.comm_sms, chunks=2)
+    x = blk.x
+    evs = []  # (name, start, end) of every GEMM launch in the timed region (N = 1)
 
     def step(record=False, xin=None, need_result=False):
-        xin = x if xin is None else xin
-        for name in ("qkv", "out", "up", "down"):
-            l = lin[name]
-            inp = out["up"] if name == "down" else xin
-            if world > 1 and l["style"] == "row":
-                main.wait_event(ar_done[name])  # previous step's reduction of this buffer
-            if record:
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-            qlinear.quantized_matmul(inp, l["wq"], l["s"], l["b"], True, gs, bits, bias=l["bias"], act=l["act"],
-                                     kernel=qlinear.KERNEL_GEMM, out=out[name], max_ctas=max_ctas)
-            if record:
-                e1.record()
-                evs.append((name, e0, e1))
-            if world > 1 and l["style"] == "row":
-                comm.wait_stream(main)
-                with torch.cuda.stream(comm):
-                    dist.all_reduce(out[name])
-                    ar_done[name].record(comm)
-        if world > 1 and need_result:
-            main.wait_event(ar_done["down"])  # the block output is complete
-        return out["down"]
+        return blk.step(xin=xin, evs=evs if record else None)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -474,8 +539,9 @@ def run_ours(args):
                              "mlp": cfg["mlp"], "bits": bits, "group_size": gs,
                              "flops_per_step": total_flops,
                              "parallelism": f"tp{world}" if world > 1 else "single",
+                             "overlap": "row-parallel linears in 2 M-slices, all-reduce of slice i overlaps the GEMM of slice i+1; each linear waits for the reduced output it reads" if world > 1 else None,
                              "l2": "no flush: each step touches ~300 MB (> 126 MB L2)"},
-                  "gpu_launches": 4 * args.steps + (0 if world == 1 else 0),
+                  "gpu_launches": blk.launches * args.steps,
                   "clocks": ck}
         if world == 1:
             # roofline of the dominant kernel (qgemm_sm100): algorithmic flops / event time per launch
@@ -516,7 +582,25 @@ def run_ours(args):
         tt = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_ms = float(tt.item())
+    # the Wan2.2-shaped block: the multi-GPU scaling workload of the path, timed
+    # at every N with the same tensor-parallel scheme
+    wan = None
+    if not args.no_extras:
+        del blk, x, xd
+        torch.cuda.empty_cache()
+        wblk = TPBlock(dict(WAN), wan_linears, dev, 4, rank, world, args.comm_sms, chunks=4)
+        wms = time_block(wblk, steps=5, warmup=2, world=world)
+        wan = {"workload": "wan2.2_q4_block_linears", "value": wblk.flops / (wms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "ms_per_step": wms, "n_gpus": world, "M": WAN["M"], "flops_per_step": wblk.flops,
+               "parallelism": f"tp{world}" if world > 1 else "single",
+               "all_reduces_per_step": 3 if world > 1 else 0, "chunks_per_row_linear": wblk.chunks,
+               "gpu_launches_per_step": wblk.launches}
+        assert qlinear.device_error() == 0, "a kernel reported a device-side error"
+        del wblk
+        torch.cuda.empty_cache()
     if rank == 0:
+        if wan is not None:
+            result["wan_block"] = wan
         result["e2e"] = {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                          "h2d_bytes_per_step": xh.numel() * 2, "d2h_bytes_per_step": yh.numel() * 2,
                          "ms_per_step": e2e_ms,
