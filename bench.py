@@ -12,8 +12,8 @@ Each step touches ~300 MB (> the 126 MB L2), so no explicit L2 flush is needed.
 
 N > 1 GPUs (torchrun, one rank per GPU, NCCL): Megatron tensor parallelism of the same
 block -- QKV / up column-parallel, out / down row-parallel with one all-reduce each, run
-in M-slices so a slice's all-reduce overlaps the next slice's GEMM, every linear waiting
-for the reduced output it reads -- so total work is fixed ("scaling": "strong").
+in M-slices that overlap the neighbouring GEMM slices, every GEMM reading the reduced
+data -- so total work is fixed ("scaling": "strong").
 
 Also reported (rank 0, N = 1):
   * "roofline": the tcgen05 GEMM kernel's achieved TFLOP/s (algorithmic 2*M*N*K per
@@ -360,13 +360,16 @@ def other_configs(dev, iters=5):
 class TPBlock:
     """The linears of one DiT block, Megatron-sharded over the ranks (N = 1: unsharded).
 
-    Column-parallel linears hold N/world packed rows; row-parallel ones hold K/world
-    (group-aligned) and are followed by an NCCL all-reduce of their output.  A row-parallel
-    linear runs in `chunks` slices of M: the all-reduce of slice i (second stream) overlaps
-    the GEMM of slice i + 1, and the next linear starts only after the last reduction -- the
-    data dependency of a real forward pass.  The GEMMs leave `comm_sms` SMs to NCCL."""
+    Column-parallel linears hold N/world packed rows, row-parallel ones K/world (group
+    aligned); each row-parallel output is reduced over the ranks by NCCL on a second
+    stream, in M-slices: the reduction of slice i overlaps the GEMM of slice i + 1, and the
+    linear that reads the output starts its slice i as soon as that slice is reduced --
+    every GEMM reads exactly the reduced data a real forward pass would give it.
+    mode "allreduce": one all-reduce per slice.  mode "seqpar" (sequence parallel): the
+    slice is reduce-scattered over the token rows and all-gathered back for the consumer
+    (same bytes, two shorter collectives).  The GEMMs leave `comm_sms` SMs to NCCL."""
 
-    def __init__(self, cfg, linears, dev, seed, rank, world, comm_sms, chunks):
+    def __init__(self, cfg, linears, dev, seed, rank, world, comm_sms, chunks, mode="allreduce"):
         import torch
         import qlinear
         from qlinear import tp
@@ -374,7 +377,6 @@ class TPBlock:
         self.cfg, self.world, self.dev = cfg, world, dev
         self.M, self.gs, self.bits = cfg["M"], cfg["gs"], cfg["bits"]
         self.spec = linears(cfg)
-        self.chunks = chunks if world > 1 else 1
         g = torch.Generator(device=dev).manual_seed(seed)
         self.lin = {}
         for name, N, K, act, style, src in self.spec:
@@ -387,22 +389,47 @@ class TPBlock:
             elif world > 1 and style == "row":
                 wq, sc, bi, _, _ = tp.row_shard(wq, sc, bi, self.gs, self.bits, rank, world)
                 if rank != 0:
-                    bias = None  # added once: the all-reduce sums rank 0's biased partial
+                    bias = None  # added once: the reduction sums rank 0's biased partial
             self.lin[name] = dict(wq=wq, s=sc, b=bi, bias=bias, act=act, style=style, src=src,
                                   N=sc.shape[0], K=sc.shape[1] * self.gs)
         self.x = torch.randn(self.M, cfg["hidden"], device=dev, generator=g).to(torch.bfloat16)
-        attn_k = next(l["K"] for l in self.lin.values() if l["src"] == "attn") if any(
-            l["src"] == "attn" for l in self.lin.values()) else 0
-        self.attn = torch.randn(self.M, attn_k, device=dev, generator=g).to(torch.bfloat16) if attn_k else None
+        attn = [l["K"] for l in self.lin.values() if l["src"] == "attn"]
+        self.attn = torch.randn(self.M, attn[0], device=dev, generator=g).to(torch.bfloat16) if attn else None
+        # local outputs (row-parallel: partial sums), and for row-parallel outputs the
+        # reduce-scattered rows of this rank and the re-gathered full tensor
         self.out = {n: torch.empty(self.M, l["N"], device=dev, dtype=torch.bfloat16) for n, l in self.lin.items()}
+        self.row = world > 1
+        if self.row:
+            if self.M % world:
+                raise ValueError("M must be a multiple of the GPU count")
+            unit = 32 * world
+            step = (self.M + chunks - 1) // chunks
+            step = (step + unit - 1) // unit * unit
+            self.bounds = [(r0, min(self.M, r0 + step)) for r0 in range(0, self.M, step)]
+        else:
+            self.bounds = [(0, self.M)]
+        self.mode = mode
+        self.shard, self.full = {}, {}
+        for n, l in self.lin.items():
+            if self.row and l["style"] == "row" and mode == "seqpar":
+                self.shard[n] = torch.empty(self.M // world, l["N"], device=dev, dtype=torch.bfloat16)
+                self.full[n] = torch.empty(self.M, l["N"], device=dev, dtype=torch.bfloat16)
+        self.reduced = {n for n, l in self.lin.items() if self.row and l["style"] == "row"}
+        self.gathered = {n for n in self.reduced if any(s_ == n for *_, s_ in self.spec)}
         self.main = torch.cuda.current_stream(dev)
-        self.comm = torch.cuda.Stream(dev) if world > 1 else None
+        self.comm = torch.cuda.Stream(dev) if self.row else None
         self.max_ctas = 0
-        if world > 1:
+        if self.row:
             self.max_ctas = torch.cuda.get_device_properties(dev).multi_processor_count - comm_sms
         self.flops = block_flops(cfg, linears)
-        self.launches = sum(self.chunks if l["style"] == "row" else 1 for l in self.lin.values())
+        self.launches = sum(1 if (not self.row or (l["style"] == "col" and l["src"] not in self.reduced))
+                            else len(self.bounds) for l in self.lin.values())
         torch.cuda.synchronize()
+
+    def result_rows(self):
+        """(tensor, rows) holding this rank's part of the block output."""
+        last = self.spec[-1][0]
+        return (self.shard[last], self.M // self.world) if last in self.shard else (self.out[last], self.M)
 
     def step(self, xin=None, evs=None):
         import torch
@@ -410,15 +437,18 @@ class TPBlock:
         import qlinear
 
         xin = self.x if xin is None else xin
+        W = self.world
+        gathered_ev = {}
         for name, _, _, _, _, src in self.spec:
             l = self.lin[name]
-            inp = xin if src == "x" else (self.attn if src == "attn" else self.out[src])
             y = self.out[name]
-            row = self.world > 1 and l["style"] == "row"
-            n = self.chunks if row else 1
-            step_m = (self.M + n - 1) // n
-            for c in range(n):
-                r0, r1 = c * step_m, min(self.M, (c + 1) * step_m)
+            from_red = src in self.reduced
+            inp = xin if src == "x" else (self.attn if src == "attn" else
+                                          (self.full[src] if src in self.full else self.out[src]))
+            sliced = self.row and (l["style"] == "row" or from_red)
+            for c, (r0, r1) in enumerate(self.bounds if sliced else [(0, self.M)]):
+                if from_red:
+                    self.main.wait_event(gathered_ev[src][c])  # rows r0:r1 of the input are reduced
                 if evs is not None:
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record()
@@ -428,13 +458,23 @@ class TPBlock:
                 if evs is not None:
                     e1.record()
                     evs.append((name, e0, e1))
-                if row:
+                if self.row and l["style"] == "row":
+                    ev = torch.cuda.Event()
                     self.comm.wait_stream(self.main)
                     with torch.cuda.stream(self.comm):
-                        dist.all_reduce(y[r0:r1])
-            if row:
-                self.main.wait_stream(self.comm)  # the consumer reads the reduced output
-        return self.out[self.spec[-1][0]]
+                        if self.mode == "seqpar":
+                            dist.reduce_scatter_tensor(self.shard[name][r0 // W:r1 // W], y[r0:r1])
+                            if name in self.gathered:
+                                dist.all_gather_into_tensor(self.full[name][r0:r1],
+                                                            self.shard[name][r0 // W:r1 // W])
+                        else:
+                            dist.all_reduce(y[r0:r1])
+                        ev.record(self.comm)
+                    gathered_ev.setdefault(name, []).append(ev)
+        if self.row:
+            self.main.wait_stream(self.comm)  # the block output's last slice is reduced
+        t, _ = self.result_rows()
+        return t
 
 
 def time_block(blk, steps, warmup, world):
@@ -539,7 +579,7 @@ def run_ours(args):
                              "mlp": cfg["mlp"], "bits": bits, "group_size": gs,
                              "flops_per_step": total_flops,
                              "parallelism": f"tp{world}" if world > 1 else "single",
-                             "overlap": "row-parallel linears in 2 M-slices, all-reduce of slice i overlaps the GEMM of slice i+1; each linear waits for the reduced output it reads" if world > 1 else None,
+                             "overlap": "row-parallel outputs all-reduced in 2 M-slices on a second stream, overlapping the next slice's GEMM; the consumer's slice i starts once slice i is reduced" if world > 1 else None,
                              "l2": "no flush: each step touches ~300 MB (> 126 MB L2)"},
                   "gpu_launches": blk.launches * args.steps,
                   "clocks": ck}
@@ -557,24 +597,25 @@ def run_ours(args):
                                   "traffic": 175331072, "traffic_launch": "up (ncu dram read+write, profiles/qgemm_flux_up_q8_traffic.md; algorithmic 180.4 MB)",
                                   "kernel": "qgemm_sm100 (4 launches/step, mean ms each)",
                                   "per_launch_ms": {k: statistics.mean(v) for k, v in per.items()}}
-    # e2e through the public API with host buffers
-    xh = x.cpu().pin_memory()
-    yh = torch.empty(M, cfg["hidden"], dtype=torch.bfloat16).pin_memory()
+    # e2e through the public API with host buffers.  N > 1: every rank moves 1/N of the rows
+    # over its own PCIe link -- its slice of x up (then an NCCL all-gather over NVLink gives
+    # every rank the whole input) and its slice of the block output down
+    rows = M // world
+    xh = x[rank * rows:(rank + 1) * rows].cpu().pin_memory()
+    out_t, out_rows = blk.result_rows()
+    yh = torch.empty(rows, cfg["hidden"], dtype=torch.bfloat16).pin_memory()
     xd = torch.empty_like(x)
+    xd_part = xd[rank * rows:(rank + 1) * rows]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t0.record()
     for _ in range(args.steps):
-        # N > 1: the input crosses PCIe once (rank 0) and reaches the other ranks by an NCCL
-        # broadcast over NVLink; the all-reduced output is read back by rank 0 only
-        if rank == 0:
-            xd.copy_(xh, non_blocking=True)
+        xd_part.copy_(xh, non_blocking=True)
         if world > 1:
-            dist.broadcast(xd, src=0)
+            dist.all_gather_into_tensor(xd, xd_part)
         y = step(xin=xd, need_result=True)
-        if rank == 0:
-            yh.copy_(y, non_blocking=True)
+        yh.copy_(y if out_rows < M else y[rank * rows:(rank + 1) * rows], non_blocking=True)
     t1.record()
     torch.cuda.synchronize()
     e2e_ms = t0.elapsed_time(t1) / args.steps
@@ -588,12 +629,13 @@ def run_ours(args):
     if not args.no_extras:
         del blk, x, xd
         torch.cuda.empty_cache()
-        wblk = TPBlock(dict(WAN), wan_linears, dev, 4, rank, world, args.comm_sms, chunks=4)
+        wblk = TPBlock(dict(WAN), wan_linears, dev, 4, rank, world, args.comm_sms, chunks=4, mode="seqpar")
         wms = time_block(wblk, steps=5, warmup=2, world=world)
         wan = {"workload": "wan2.2_q4_block_linears", "value": wblk.flops / (wms * 1e-3) / 1e12, "unit": "TFLOP/s",
                "ms_per_step": wms, "n_gpus": world, "M": WAN["M"], "flops_per_step": wblk.flops,
                "parallelism": f"tp{world}" if world > 1 else "single",
-               "all_reduces_per_step": 3 if world > 1 else 0, "chunks_per_row_linear": wblk.chunks,
+               "reductions_per_step": 3 if world > 1 else 0, "slices": len(wblk.bounds),
+               "tp_mode": "sequence parallel (reduce-scatter + all-gather per slice)" if world > 1 else None,
                "gpu_launches_per_step": wblk.launches}
         assert qlinear.device_error() == 0, "a kernel reported a device-side error"
         del wblk
@@ -602,10 +644,11 @@ def run_ours(args):
         if wan is not None:
             result["wan_block"] = wan
         result["e2e"] = {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                         "h2d_bytes_per_step": xh.numel() * 2, "d2h_bytes_per_step": yh.numel() * 2,
+                         "h2d_bytes_per_step": M * cfg["hidden"] * 2, "d2h_bytes_per_step": M * cfg["hidden"] * 2,
                          "ms_per_step": e2e_ms,
                          "path": "pinned H2D of x and D2H of the block output inside the timed region"
-                                 + ("; x broadcast from rank 0 over NCCL" if world > 1 else "")}
+                                 + ("; each rank copies 1/N of the rows each way, x all-gathered over NCCL"
+                                    if world > 1 else "")}
         if world == 1 and not args.no_extras:
             result["cpu_baseline"] = cpu_baseline_sample(cfg)
             result["decode_gemv"] = decode_gemv(dev)
