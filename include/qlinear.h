@@ -86,6 +86,13 @@ typedef struct {
     int kernel;                /* ql_kernel (QL_KERNEL_AUTO unless testing a path)     */
     int max_ctas;              /* GEMM: cap on resident CTAs (0 = one per SM); leaves
                                   SMs free for a collective running alongside          */
+    /* Gated residual (the DiT blocks' `x + gate * linear(x)`, src/nn.rs:166-176):
+       y = residual + gate * f(x W^T + bias), each op rounded to y's dtype.  NULL residual:
+       off.  gate [rows, N] with row m / gate_period (gate_period 0: one row for all M);
+       NULL gate: y = residual + f(...).  Both in y's dtype; residual may alias y.      */
+    const void *residual;      /* [M, N]                                               */
+    const void *gate;          /* [M / gate_period, N] or [N]                          */
+    int64_t gate_period;       /* token rows per gate row (0: one gate row)            */
 } ql_epilogue;
 
 /* Library version (major*10000 + minor*100 + patch). */

@@ -35,18 +35,19 @@ int launch_dequantize(const int64_t *, int64_t, int64_t, int64_t, int, int, cons
                       const void *, const void *, int, void *, int, cudaStream_t);
 int launch_qgemv(const void *, int64_t, int64_t, const uint32_t *, const void *, const void *,
                  const uint32_t *, const void *, const void *, int64_t, int, int, const void *,
-                 const void *, int, const void *, const void *, int64_t, void *, cudaStream_t);
+                 const void *, int, const void *, const void *, int64_t, void *, const Gated &, cudaStream_t);
 bool qgemv_tc_supported(int64_t, int64_t, int, int, const void *, bool);
 int launch_qgemv_tc(const void *, int64_t, int64_t, const uint32_t *, const void *, const void *, const uint32_t *,
                     const void *, const void *, int64_t, int, int, const void *, const void *, int, void *,
-                    cudaStream_t);
+                    const Gated &, cudaStream_t);
 int launch_qgemm_sm100(const void *, int64_t, int64_t, const uint32_t *, const void *, const void *,
                        const uint32_t *, const void *, const void *, int64_t, int, int, const void *,
-                       const void *, int, const void *, const void *, int64_t, void *, int, int, cudaStream_t);
+                       const void *, int, const void *, const void *, int64_t, void *, int, int, const Gated &,
+                       cudaStream_t);
 int launch_qmm_generic(const void *, int, int64_t, int64_t, const uint32_t *, const void *,
                        const void *, const uint32_t *, const void *, const void *, int, int64_t, int,
                        int, const void *, const void *, int, const void *, const void *, int64_t,
-                       float, void *, int, cudaStream_t);
+                       float, void *, int, const Gated &, cudaStream_t);
 int launch_lora_t(const void *, int64_t, int64_t, const void *, int64_t, float, void *, cudaStream_t);
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -168,6 +169,9 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
     if (lora && e.lora_rank > 4096) return fail(QL_EUNSUPPORTED, "LoRA rank > 4096");
 
     const bool tc_dtypes = x_dtype == QL_BF16 && sb_dtype == QL_BF16 && y_dtype == QL_BF16;
+    if (e.gate && !e.residual) return fail(QL_EINVAL_ARG, "a gate needs a residual");
+    if (e.gate_period < 0) return fail(QL_EINVAL_ARG, "gate_period must be >= 0");
+    const Gated gd{e.residual, e.gate, e.gate_period};
     int kernel = e.kernel;
     if (kernel == QL_KERNEL_AUTO) kernel = !tc_dtypes ? QL_KERNEL_GENERIC : (M <= 8 ? QL_KERNEL_GEMV : QL_KERNEL_GEMM);
     if (kernel != QL_KERNEL_GENERIC && !tc_dtypes)
@@ -180,14 +184,14 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
             !aligned16(scales) || !aligned16(biases) || (swiglu && (!aligned16(e.scales_up) || !aligned16(e.biases_up))))
             return fail(QL_EUNSUPPORTED, "tcgen05 GEMV: unsupported shape, group size or LoRA");
         return launch_qgemv_tc(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size, bits,
-                               e.bias, e.bias_up, e.act, y, st);
+                               e.bias, e.bias_up, e.act, y, gd, st);
     }
 
     if (kernel == QL_KERNEL_GENERIC)
         return launch_qmm_generic(x, x_dtype, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up,
                                   sb_dtype, N, group_size, bits, e.bias, e.bias_up, e.act,
                                   lora ? e.lora_a : nullptr, e.lora_b, lora ? e.lora_rank : 0,
-                                  e.lora_scale, y, y_dtype, st);
+                                  e.lora_scale, y, y_dtype, gd, st);
 
     const void *lora_t = nullptr;
     if (lora) {
@@ -200,10 +204,10 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
     }
     if (kernel == QL_KERNEL_GEMV)
         return launch_qgemv(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size,
-                            bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y, st);
+                            bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y, gd, st);
     return launch_qgemm_sm100(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size,
                               bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y,
-                              kernel == QL_KERNEL_GEMM_PAIR ? 2 : 1, e.max_ctas, st);
+                              kernel == QL_KERNEL_GEMM_PAIR ? 2 : 1, e.max_ctas, gd, st);
 }
 
 }  // extern "C"

@@ -100,6 +100,7 @@ struct Params {
     const __nv_bfloat16 *lora_b;             // [rank, N]
     int lora_rank;
     __nv_bfloat16 *y;
+    Gated gd;                                // gated residual epilogue
 };
 
 __device__ __forceinline__ float gelu_tanh_f(float x) {
@@ -350,7 +351,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             const int m = m0 + c * 32 + i;
                             const float g = (i & 1) ? bf16hi(pk[i >> 1]) : bf16lo(pk[i >> 1]);
                             const float u = xch[row * 33 + i];
-                            if (m < p.M) p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(silu_f(g) * u);
+                            if (m < p.M)
+                                p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(apply_gated(silu_f(g) * u, p.gd, m, n, p.N));
                         }
                     }
                     named_bar_sync(1, 128);
@@ -361,7 +363,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         float v = (i & 1) ? bf16hi(pk[i >> 1]) : bf16lo(pk[i >> 1]);
                         if (p.act == QL_ACT_GELU_TANH) v = gelu_tanh_f(v);
                         else if (p.act == QL_ACT_GELU_ERF) v = gelu_erf_f(v);
-                        if (m < p.M) p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(v);
+                        if (m < p.M) p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(apply_gated(v, p.gd, m, n, p.N));
                     }
                 }
             }
@@ -615,11 +617,12 @@ int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, 
                        const void *biases, const uint32_t *wq2, const void *scales2,
                        const void *biases2, int64_t N, int gs, int bits, const void *bias,
                        const void *bias2, int act, const void *lora_t, const void *lora_b,
-                       int64_t rank, void *y, int cg, int max_ctas, cudaStream_t st) {
+                       int64_t rank, void *y, int cg, int max_ctas, const Gated &gd, cudaStream_t st) {
     using namespace gemm;
     const bool swiglu = act == QL_ACT_SWIGLU;
     const int wrows = (swiglu ? 64 : BW) * cg;  // output columns per tile
     Params p{};
+    p.gd = gd;
     p.M = (int)M;
     p.N = (int)N;
     p.K = (int)K;

@@ -40,6 +40,7 @@ struct Params {
     int rank, rpad;
     int act;
     __nv_bfloat16 *y;
+    Gated gd;
 };
 
 __device__ __forceinline__ void mma16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
@@ -264,7 +265,7 @@ __global__ void __launch_bounds__(WARPS * 32, 2) qgemv_kernel(const Params p) {
                 } else if (p.act == QL_ACT_GELU_ERF) {
                     v = 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
                 }
-                p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(v);
+                p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(apply_gated(v, p.gd, m, n, p.N));
             }
         }
         __syncthreads();
@@ -277,12 +278,12 @@ bool qgemv_tma_supported(int64_t M, int64_t K, int gs);
 int launch_qgemv_tma(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales,
                      const void *biases, const uint32_t *wq2, const void *scales2, const void *biases2,
                      int64_t N, int gs, int bits, const void *bias, const void *bias2, int act,
-                     const void *lora_t, const void *lora_b, int64_t rank, void *y, cudaStream_t st);
+                     const void *lora_t, const void *lora_b, int64_t rank, void *y, const Gated &gd, cudaStream_t st);
 
 bool qgemv_tc_supported(int64_t M, int64_t K, int gs, int bits, const void *x, bool lora);
 int launch_qgemv_tc(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales, const void *biases,
                     const uint32_t *wq2, const void *scales2, const void *biases2, int64_t N, int gs, int bits,
-                    const void *bias, const void *bias2, int act, void *y, cudaStream_t st);
+                    const void *bias, const void *bias2, int act, void *y, const Gated &gd, cudaStream_t st);
 
 static bool all_aligned16(std::initializer_list<const void *> ps) {
     for (const void *p : ps)
@@ -293,7 +294,7 @@ static bool all_aligned16(std::initializer_list<const void *> ps) {
 int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales,
                  const void *biases, const uint32_t *wq2, const void *scales2, const void *biases2,
                  int64_t N, int gs, int bits, const void *bias, const void *bias2, int act,
-                 const void *lora_t, const void *lora_b, int64_t rank, void *y, cudaStream_t st) {
+                 const void *lora_t, const void *lora_b, int64_t rank, void *y, const Gated &gd, cudaStream_t st) {
     // the tcgen05 kernel (qgemv_tc.cu) when the shape allows it, else the TMA-fed
     // mma.sync kernel (qgemv_tma.cu), else the register-fed one below
     static const bool force_regs = getenv("QL_GEMV_REGS") != nullptr;  // profiling switches
@@ -313,12 +314,13 @@ int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const 
     if (!force_regs && !force_mma && (force_tc || tiles >= n_sms || M >= 6) &&
         qgemv_tc_supported(M, K, gs, bits, x, lora_t != nullptr) && all_aligned16({scales, biases, scales2, biases2}))
         return launch_qgemv_tc(x, M, K, wq, scales, biases, wq2, scales2, biases2, N, gs, bits, bias, bias2, act, y,
-                               st);
+                               gd, st);
     if (!force_regs && qgemv_tma_supported(M, K, gs))
         return launch_qgemv_tma(x, M, K, wq, scales, biases, wq2, scales2, biases2, N, gs, bits, bias, bias2, act,
-                                lora_t, lora_b, rank, y, st);
+                                lora_t, lora_b, rank, y, gd, st);
     using namespace gemv;
     Params p{};
+    p.gd = gd;
     p.x = (const __nv_bfloat16 *)x;
     p.M = (int)M;
     p.N = (int)N;

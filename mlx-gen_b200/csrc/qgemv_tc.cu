@@ -79,6 +79,7 @@ struct Params {
     int act;
     const __nv_bfloat16 *x, *bias, *bias2;
     __nv_bfloat16 *y;
+    Gated gd;
 };
 
 __device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
@@ -612,8 +613,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         for (int t = 0; t < 8; ++t)
                             if (t < p.M) {
                                 const float g = v8[t];
-                                p.y[(int64_t)t * p.N + n] =
-                                    __float2bfloat16_rn(g / (1.0f + __expf(-g)) * xch[row * 8 + t]);
+                                p.y[(int64_t)t * p.N + n] = __float2bfloat16_rn(
+                                    apply_gated(g / (1.0f + __expf(-g)) * xch[row * 8 + t], p.gd, t, n, p.N));
                             }
                     mbar_arrive(xchfree);
                 }
@@ -630,7 +631,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         } else if (p.act == QL_ACT_GELU_ERF) {
                             v = 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
                         }
-                        p.y[(int64_t)t * p.N + n] = __float2bfloat16_rn(v);
+                        p.y[(int64_t)t * p.N + n] = __float2bfloat16_rn(apply_gated(v, p.gd, t, n, p.N));
                     }
             }
         }
@@ -740,10 +741,11 @@ bool qgemv_tc_supported(int64_t M, int64_t K, int gs, int bits, const void *x, b
 
 int launch_qgemv_tc(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales, const void *biases,
                     const uint32_t *wq2, const void *scales2, const void *biases2, int64_t N, int gs, int bits,
-                    const void *bias, const void *bias2, int act, void *y, cudaStream_t st) {
+                    const void *bias, const void *bias2, int act, void *y, const Gated &gd, cudaStream_t st) {
     using namespace gemv3;
     const bool sw = act == QL_ACT_SWIGLU;
     Params p{};
+    p.gd = gd;
     p.M = (int)M;
     p.N = (int)N;
     p.K = (int)K;

@@ -41,6 +41,7 @@ struct Params {
     const __nv_bfloat16 *lora_t, *lora_b;
     int rank, rpad;
     __nv_bfloat16 *y;
+    Gated gd;
 };
 
 template <int BITS, bool SWIGLU>
@@ -361,7 +362,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                 } else if (p.act == QL_ACT_GELU_ERF) {
                     v = 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
                 }
-                p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(v);
+                p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(apply_gated(v, p.gd, m, n, p.N));
             }
         }
     }
@@ -424,10 +425,11 @@ bool qgemv_tma_supported(int64_t M, int64_t K, int gs) { return M >= 1 && M <= 8
 int launch_qgemv_tma(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales,
                      const void *biases, const uint32_t *wq2, const void *scales2, const void *biases2,
                      int64_t N, int gs, int bits, const void *bias, const void *bias2, int act,
-                     const void *lora_t, const void *lora_b, int64_t rank, void *y, cudaStream_t st) {
+                     const void *lora_t, const void *lora_b, int64_t rank, void *y, const Gated &gd, cudaStream_t st) {
     using namespace gemv2;
     const bool sw = act == QL_ACT_SWIGLU;
     Params p{};
+    p.gd = gd;
     p.M = (int)M;
     p.N = (int)N;
     p.K = (int)K;

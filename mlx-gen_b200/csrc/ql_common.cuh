@@ -116,6 +116,28 @@ __device__ __forceinline__ float q8_code_f32(uint32_t w, int byte) {
     return __uint_as_float(f) - 8388608.0f;
 }
 
+// Gated residual epilogue, y = residual + gate * f(x W^T + bias), each op rounded to bf16
+// as the reference's eager `add(x, multiply(gate, y))` does (src/nn.rs:166-176).
+// res: [M, N] (NULL: no residual), gate: [M / period, N] (NULL: no gate; period 0: one
+// gate row for every token row), both bf16.
+struct Gated {
+    const void *res;
+    const void *gate;
+    int64_t period;
+};
+
+// v: the linear's final value (after bias and activation, not yet rounded); returns the
+// value to round to bf16 and store.
+__device__ __forceinline__ float apply_gated(float v, const Gated &g, int64_t m, int64_t n, int64_t N) {
+    if (!g.res) return v;
+    float y = round_bf16(v);
+    if (g.gate) {
+        const int64_t gr = g.period > 0 ? m / g.period : 0;
+        y = round_bf16(__bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(g.gate)[gr * N + n]) * y);
+    }
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(g.res)[m * N + n]) + y;
+}
+
 // ------------------------------------------------------------------ mbarrier
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {

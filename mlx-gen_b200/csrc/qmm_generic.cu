@@ -35,6 +35,7 @@ struct Params {
     int act;
     void *y;
     int ydt;
+    Gated gd;  // residual and gate in y's dtype
 };
 
 __device__ __forceinline__ float act_f(float v, int act) {
@@ -105,6 +106,14 @@ __global__ void __launch_bounds__(256) qmm_generic_kernel(const Params p) {
                 v = v / (1.0f + expf(-v)) * u;
             } else {
                 v = act_f(v, p.act);
+            }
+            if (p.gd.res) {  // gated residual, each op rounded to y's dtype
+                v = round_to(p.ydt, v);
+                if (p.gd.gate) {
+                    const int64_t gr = p.gd.period > 0 ? m / p.gd.period : 0;
+                    v = round_to(p.ydt, load_as_f32(p.gd.gate, p.ydt, gr * p.N + n) * v);
+                }
+                v = load_as_f32(p.gd.res, p.ydt, (int64_t)m * p.N + n) + v;
             }
             store_from_f32(p.y, p.ydt, (int64_t)m * p.N + n, v);
         }
@@ -228,9 +237,7 @@ __global__ void __launch_bounds__(128) lora_t_mma_kernel(const __grid_constant__
         else
             cp_async_wait<ST - 2>();
         __syncthreads();  // chunk kc landed for every thread; stage (kc - 1) % ST is free
-#ifndef QL_EXP_LT_NOLOAD
         if (kc + ST - 1 < nk) load(kc + ST - 1, (kc + ST - 1) % ST);
-#endif
         cp_async_commit();
         const int s = kc % ST;
         const uint32_t xb = smem_u32(sx[s]), ab = smem_u32(sa[s]);
@@ -242,13 +249,8 @@ __global__ void __launch_bounds__(128) lora_t_mma_kernel(const __grid_constant__
             for (int h = 0; h < NH; ++h) {
                 uint32_t bf[4];
                 ldsm_x4_t(ab + swz(16 * kk + (lane & 15), 2 * NH * wn + 2 * h + (lane >> 4)), bf);
-#ifndef QL_EXP_LT_NOMMA
                 mma_bf16(acc[2 * h], af, bf[0], bf[1]);
                 mma_bf16(acc[2 * h + 1], af, bf[2], bf[3]);
-#else
-                acc[2 * h][0] += __uint_as_float(af[0] ^ bf[0]);
-                acc[2 * h + 1][0] += __uint_as_float(af[1] ^ bf[2]);
-#endif
             }
         }
     }
@@ -278,8 +280,9 @@ int launch_qmm_generic(const void *x, int xdt, int64_t M, int64_t K, const uint3
                        const void *scales2, const void *biases2, int sdt, int64_t N, int gs,
                        int bits, const void *bias, const void *bias2, int act, const void *lora_a,
                        const void *lora_b, int64_t rank, float lora_scale, void *y, int ydt,
-                       cudaStream_t st) {
+                       const Gated &gd, cudaStream_t st) {
     generic::Params p{};
+    p.gd = gd;
     p.x = x;
     p.xdt = xdt;
     p.M = (int)M;

@@ -68,6 +68,9 @@ class Epilogue(C.Structure):
         ("workspace_bytes", C.c_size_t),
         ("kernel", C.c_int),
         ("max_ctas", C.c_int),
+        ("residual", C.c_void_p),
+        ("gate", C.c_void_p),
+        ("gate_period", C.c_int64),
     ]
 
 

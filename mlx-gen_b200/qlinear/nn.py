@@ -64,9 +64,13 @@ class QuantizedLinear:
         return [self.scales.shape[0], self.scales.shape[1] * self.group_size]
 
     def forward(self, x: torch.Tensor, *, act: Optional[str] = None, lora=None,
-                kernel: int = KERNEL_AUTO) -> torch.Tensor:
+                kernel: int = KERNEL_AUTO, residual: Optional[torch.Tensor] = None,
+                gate: Optional[torch.Tensor] = None, gate_period: int = 0) -> torch.Tensor:
+        """``residual``/``gate`` fuse the DiT blocks' gated residual ``residual + gate * y``
+        (the reference's ``nn::gated``, src/nn.rs:166-176) into the epilogue."""
         return ops.quantized_matmul(x, self.weight, self.scales, self.biases, True, self.group_size,
-                                    self.bits, bias=self.bias, act=act, lora=lora, kernel=kernel)
+                                    self.bits, bias=self.bias, act=act, lora=lora, kernel=kernel,
+                                    residual=residual, gate=gate, gate_period=gate_period)
 
 
 @dataclass

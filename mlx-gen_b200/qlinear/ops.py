@@ -103,7 +103,8 @@ def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, bi
                      up: Optional[Sequence[Optional[torch.Tensor]]] = None,
                      lora: Optional[tuple] = None, workspace: Optional[torch.Tensor] = None,
                      kernel: int = KERNEL_AUTO, out: Optional[torch.Tensor] = None,
-                     max_ctas: int = 0) -> torch.Tensor:
+                     max_ctas: int = 0, residual: Optional[torch.Tensor] = None,
+                     gate: Optional[torch.Tensor] = None, gate_period: int = 0) -> torch.Tensor:
     """``y = x . dequant(W)^T`` (+ fused epilogue), like ``mlx_rs::ops::quantized_matmul``
     with ``transpose=true`` followed by the ops the reference runs after it.
 
@@ -111,7 +112,9 @@ def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, bi
     src/adapters.rs:318-320 does).  act: None, "gelu_tanh", "gelu" or "swiglu" (then
     ``up = (wq3, scales3, biases3[, bias3])`` is the second projection and the result is
     ``silu(x W^T) * (x W3^T)``).  lora: ``(A [K, r], B [r, N], scale)`` adds
-    ``scale * (x.A).B``.  Output dtype = x's dtype."""
+    ``scale * (x.A).B``.  residual / gate: the gated residual ``residual + gate * y``
+    (src/nn.rs:166-176), gate ``[N]`` or ``[M / gate_period, N]``.  Output dtype = x's
+    dtype."""
     _need_cuda(x, wq, scales, biases, bias)
     if not transpose:
         raise NotImplementedError("only transpose=True is supported (the reference's only form)")
@@ -152,6 +155,17 @@ def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, bi
         keep.append(workspace)
         ep.workspace = workspace.data_ptr()
         ep.workspace_bytes = workspace.numel() * workspace.element_size()
+    if residual is not None:
+        residual = residual.to(y.dtype).reshape(-1, N).contiguous()
+        keep.append(residual)
+        ep.residual = residual.data_ptr()
+        if gate is not None:
+            gate = gate.to(y.dtype).reshape(-1, N).contiguous()
+            keep.append(gate)
+            ep.gate = gate.data_ptr()
+            ep.gate_period = int(gate_period)
+    elif gate is not None:
+        raise ValueError("a gate needs a residual")
     ep.kernel = kernel
     ep.max_ctas = max_ctas
     check(lib().ql_quantized_matmul(_ptr(x2), dtype_code(x2), M, K, _ptr(wq.contiguous()),

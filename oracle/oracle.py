@@ -161,3 +161,17 @@ def swiglu(a, b):
     out = np.empty_like(a)
     lib().qref_swiglu(_p(a), _p(b), a.size, dtype_code(a), _p(out))
     return out
+
+
+def gated(res, gate, y, period=0):
+    """``res + gate * y`` with each op rounded to bf16, as the reference's eager
+    ``add(x, multiply(gate, y))`` on bf16 arrays (src/nn.rs:166-176).  All bf16 bits;
+    gate is [N] or [rows, N] with row m // period (period 0: row 0 for every m)."""
+    y32 = bf16_to_f32(np.ascontiguousarray(y))
+    M, N = y32.shape
+    if gate is not None:
+        g = bf16_to_f32(np.ascontiguousarray(gate)).reshape(-1, N)
+        rows = (np.arange(M) // period) if period > 0 else np.zeros(M, np.int64)
+        y32 = bf16_to_f32(to_bf16(g[rows] * y32))
+    return to_bf16(bf16_to_f32(np.ascontiguousarray(res)) + y32)
+

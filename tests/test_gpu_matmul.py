@@ -238,3 +238,31 @@ def test_gemv_tc_parity(dev, bits, gs, M, K):
     torch.cuda.synchronize()
     assert qlinear.device_error() == 0
     assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(O.quantized_matmul(x, wq, s, b, gs, bits)), what="gemv-tc")
+
+
+@pytest.mark.parametrize("kernel,M", [(GEMV, 1), (GEMV, 5), (GEMV_TC, 3), (GEMM, 300), (GEMM2, 300),
+                                      (GENERIC, 7)])
+@pytest.mark.parametrize("gate_mode", ["none", "row", "period"])
+def test_gated_residual_epilogue(dev, kernel, M, gate_mode):
+    """y = residual + gate * (x W^T + bias) fused in the epilogue, each op rounded to bf16
+    as the reference's eager ops (src/nn.rs:166-176); gate per column, or per batch of
+    `period` token rows."""
+    N, K, gs, bits = 256, 1024, 64, 4
+    rng, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 41 + M)
+    bias = rand_bf16((N,), 0.2, rng)
+    res = rand_bf16((M, N), 1.0, rng)
+    gate, period = None, 0
+    if gate_mode == "row":
+        gate = rand_bf16((N,), 1.0, rng)
+    elif gate_mode == "period":
+        period = 2
+        gate = rand_bf16(((M + period - 1) // period, N), 1.0, rng)
+    y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, bias=np2t(bias, dev), kernel=kernel,
+                                 residual=np2t(res, dev), gate=None if gate is None else np2t(gate, dev),
+                                 gate_period=period)
+    torch.cuda.synchronize()
+    assert qlinear.device_error() == 0
+    lin = O.quantized_matmul(x, wq, s, b, gs, bits, bias=bias)
+    ref = O.gated(res, gate, lin, period)
+    # the linear's own tolerance, carried through the gate (|gate| ~ 1) and the residual add
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), ulps=4, what=f"gated {gate_mode}")
