@@ -60,6 +60,9 @@ typedef enum {
     QL_KERNEL_GEMM_PAIR = 4, /* the same GEMM on CTA pairs (cta_group::2); slower today */
     QL_KERNEL_GEMV_TC = 5, /* the tcgen05 GEMV alone (M <= 8, no LoRA, group 64/128 or Q8/32;
                               QL_EUNSUPPORTED otherwise); QL_KERNEL_GEMV picks it for wide N */
+    QL_KERNEL_GEMV_TMA = 6, /* the TMA-fed mma.sync GEMV alone (M <= 8, K a whole number of
+                               8-group batches)                                          */
+    QL_KERNEL_GEMV_REGS = 7, /* the register-fed GEMV alone (M <= 8)                     */
 } ql_kernel;
 
 /* Fused epilogue and options of ql_quantized_matmul.  Zero-initialise, then set

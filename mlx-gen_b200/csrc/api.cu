@@ -35,7 +35,7 @@ int launch_dequantize(const int64_t *, int64_t, int64_t, int64_t, int, int, cons
                       const void *, const void *, int, void *, int, cudaStream_t);
 int launch_qgemv(const void *, int64_t, int64_t, const uint32_t *, const void *, const void *,
                  const uint32_t *, const void *, const void *, int64_t, int, int, const void *,
-                 const void *, int, const void *, const void *, int64_t, void *, const Gated &, cudaStream_t);
+                 const void *, int, const void *, const void *, int64_t, void *, const Gated &, int, cudaStream_t);
 bool qgemv_tc_supported(int64_t, int64_t, int, int, const void *, bool);
 int launch_qgemv_tc(const void *, int64_t, int64_t, const uint32_t *, const void *, const void *, const uint32_t *,
                     const void *, const void *, int64_t, int, int, const void *, const void *, int, void *,
@@ -176,9 +176,10 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
     if (kernel == QL_KERNEL_AUTO) kernel = !tc_dtypes ? QL_KERNEL_GENERIC : (M <= 8 ? QL_KERNEL_GEMV : QL_KERNEL_GEMM);
     if (kernel != QL_KERNEL_GENERIC && !tc_dtypes)
         return fail(QL_EUNSUPPORTED, "tensor-core kernels need bf16 x, scales and y");
-    if ((kernel == QL_KERNEL_GEMV || kernel == QL_KERNEL_GEMV_TC) && M > 8)
+    if ((kernel == QL_KERNEL_GEMV || kernel == QL_KERNEL_GEMV_TC || kernel == QL_KERNEL_GEMV_TMA ||
+         kernel == QL_KERNEL_GEMV_REGS) && M > 8)
         return fail(QL_EUNSUPPORTED, "GEMV kernel needs M <= 8");
-    if (kernel < QL_KERNEL_AUTO || kernel > QL_KERNEL_GEMV_TC) return fail(QL_EINVAL_ARG, "unknown kernel %d", kernel);
+    if (kernel < QL_KERNEL_AUTO || kernel > QL_KERNEL_GEMV_REGS) return fail(QL_EINVAL_ARG, "unknown kernel %d", kernel);
     if (kernel == QL_KERNEL_GEMV_TC) {
         if (lora || !qgemv_tc_supported(M, K, group_size, bits, x, false) ||
             !aligned16(scales) || !aligned16(biases) || (swiglu && (!aligned16(e.scales_up) || !aligned16(e.biases_up))))
@@ -202,9 +203,10 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
         if (int rc = launch_lora_t(x, M, K, e.lora_a, e.lora_rank, e.lora_scale, e.workspace, st)) return rc;
         lora_t = e.workspace;
     }
-    if (kernel == QL_KERNEL_GEMV)
+    if (kernel == QL_KERNEL_GEMV || kernel == QL_KERNEL_GEMV_TMA || kernel == QL_KERNEL_GEMV_REGS)
         return launch_qgemv(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size,
-                            bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y, gd, st);
+                            bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y, gd,
+                            kernel == QL_KERNEL_GEMV_TMA ? 1 : kernel == QL_KERNEL_GEMV_REGS ? 2 : 0, st);
     return launch_qgemm_sm100(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size,
                               bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y,
                               kernel == QL_KERNEL_GEMM_PAIR ? 2 : 1, e.max_ctas, gd, st);

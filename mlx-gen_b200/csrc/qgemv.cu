@@ -294,10 +294,19 @@ static bool all_aligned16(std::initializer_list<const void *> ps) {
 int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales,
                  const void *biases, const uint32_t *wq2, const void *scales2, const void *biases2,
                  int64_t N, int gs, int bits, const void *bias, const void *bias2, int act,
-                 const void *lora_t, const void *lora_b, int64_t rank, void *y, const Gated &gd, cudaStream_t st) {
-    // the tcgen05 kernel (qgemv_tc.cu) when the shape allows it, else the TMA-fed
-    // mma.sync kernel (qgemv_tma.cu), else the register-fed one below
-    static const bool force_regs = getenv("QL_GEMV_REGS") != nullptr;  // profiling switches
+                 const void *lora_t, const void *lora_b, int64_t rank, void *y, const Gated &gd, int which,
+                 cudaStream_t st) {
+    // which: 0 = automatic (below), 1 = the TMA-fed mma.sync kernel only, 2 = the
+    // register-fed kernel only.  Automatic: the tcgen05 kernel (qgemv_tc.cu) when the shape
+    // allows it and pays, else the TMA-fed kernel (qgemv_tma.cu), else the one below.
+    if (which == 1) {
+        if (!qgemv_tma_supported(M, K, gs))
+            return fail(QL_EUNSUPPORTED, "TMA GEMV: K must be a whole number of 8-group batches");
+        return launch_qgemv_tma(x, M, K, wq, scales, biases, wq2, scales2, biases2, N, gs, bits, bias, bias2, act,
+                                lora_t, lora_b, rank, y, gd, st);
+    }
+    static const bool env_regs = getenv("QL_GEMV_REGS") != nullptr;  // profiling switches
+    const bool force_regs = env_regs || which == 2;
     static const bool force_mma = getenv("QL_GEMV_MMA") != nullptr;
     // The tcgen05 kernel wins once its row tiles (128 rows, 64 with SwiGLU) fill the GPU,
     // or at 6+ tokens (the mma.sync kernel's per-token folds grow with M); below that its
@@ -315,7 +324,10 @@ int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const 
         qgemv_tc_supported(M, K, gs, bits, x, lora_t != nullptr) && all_aligned16({scales, biases, scales2, biases2}))
         return launch_qgemv_tc(x, M, K, wq, scales, biases, wq2, scales2, biases2, N, gs, bits, bias, bias2, act, y,
                                gd, st);
-    if (!force_regs && qgemv_tma_supported(M, K, gs))
+    // Narrow projections at M = 1 and every shape at M = 2..5 run best on the register-fed
+    // kernel below (no TMA / barrier set-up; measured on the Llama-3.2-3B decode step).
+    const bool regs_pick = (M >= 2 && M <= 5) || (act != QL_ACT_SWIGLU && N <= 4096);
+    if (!force_regs && !regs_pick && qgemv_tma_supported(M, K, gs))
         return launch_qgemv_tma(x, M, K, wq, scales, biases, wq2, scales2, biases2, N, gs, bits, bias, bias2, act,
                                 lora_t, lora_b, rank, y, gd, st);
     using namespace gemv;

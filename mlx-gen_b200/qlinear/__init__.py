@@ -6,7 +6,8 @@ dequantize / quantized_matmul``; ``AdaptableLinear``, ``Adapter``, ``TokenEmbedd
 include/qlinear.h.  All arithmetic runs in libqlinear.so (CUDA, sm_100a).
 """
 from ._lib import (ACT_GELU_ERF, ACT_GELU_TANH, ACT_NONE, ACT_SWIGLU, KERNEL_AUTO, KERNEL_GEMM, KERNEL_GEMM_PAIR,
-                   KERNEL_GEMV, KERNEL_GEMV_TC, KERNEL_GENERIC, QlError, device_error)
+                   KERNEL_GEMV, KERNEL_GEMV_REGS, KERNEL_GEMV_TC, KERNEL_GEMV_TMA, KERNEL_GENERIC, QlError,
+                   device_error)
 from .nn import (DEFAULT_GROUP_SIZE, AdaptableLinear, Linear, Lokr, Lora, QuantizedLinear,
                  TokenEmbedding)
 from .ops import dequantize, dequantize_rows, quantize, quantized_matmul, workspace_size
@@ -14,7 +15,7 @@ from .quant import embedding, lin, packed_bits, quantize_map
 
 __all__ = [
     "ACT_GELU_ERF", "ACT_GELU_TANH", "ACT_NONE", "ACT_SWIGLU", "KERNEL_AUTO", "KERNEL_GEMM", "KERNEL_GEMM_PAIR",
-    "KERNEL_GEMV", "KERNEL_GEMV_TC", "KERNEL_GENERIC", "QlError", "device_error", "DEFAULT_GROUP_SIZE",
+    "KERNEL_GEMV", "KERNEL_GEMV_REGS", "KERNEL_GEMV_TC", "KERNEL_GEMV_TMA", "KERNEL_GENERIC", "QlError", "device_error", "DEFAULT_GROUP_SIZE",
     "AdaptableLinear", "Linear", "Lokr", "Lora", "QuantizedLinear", "TokenEmbedding", "dequantize",
     "dequantize_rows", "quantize", "quantized_matmul", "workspace_size", "embedding", "lin",
     "packed_bits", "quantize_map",

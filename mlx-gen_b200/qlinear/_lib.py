@@ -17,7 +17,8 @@ LIB_PATH = os.environ.get("QL_LIB_PATH") or os.path.join(_HERE, "libqlinear.so")
 QL_F32, QL_BF16, QL_F16 = 0, 1, 2
 QL_OK, QL_EINVAL_SHAPE, QL_EUNSUPPORTED, QL_ECUDA, QL_EINVAL_ARG, QL_ETIMEOUT = range(6)
 ACT_NONE, ACT_GELU_TANH, ACT_GELU_ERF, ACT_SWIGLU = range(4)
-KERNEL_AUTO, KERNEL_GENERIC, KERNEL_GEMV, KERNEL_GEMM, KERNEL_GEMM_PAIR, KERNEL_GEMV_TC = range(6)
+(KERNEL_AUTO, KERNEL_GENERIC, KERNEL_GEMV, KERNEL_GEMM, KERNEL_GEMM_PAIR, KERNEL_GEMV_TC, KERNEL_GEMV_TMA,
+ KERNEL_GEMV_REGS) = range(8)
 
 STATUS_NAMES = {
     QL_OK: "QL_OK",

@@ -13,6 +13,7 @@ from helpers import assert_bf16_close, np2t, rand_bf16, t2np
 pytestmark = pytest.mark.gpu
 GEMV, GEMM, GENERIC = qlinear.KERNEL_GEMV, qlinear.KERNEL_GEMM, qlinear.KERNEL_GENERIC
 GEMV_TC = qlinear.KERNEL_GEMV_TC
+GEMV_TMA, GEMV_REGS = qlinear.KERNEL_GEMV_TMA, qlinear.KERNEL_GEMV_REGS
 GEMM2 = qlinear.KERNEL_GEMM_PAIR
 
 
@@ -38,12 +39,15 @@ def test_fixture_qmm_f32(golden, dev, bits):
 @pytest.mark.parametrize("gs", [32, 64, 128])
 @pytest.mark.parametrize("M", [1, 2, 3, 8])
 @pytest.mark.parametrize("K", [384, 1024, 2560])
-def test_gemv_parity(dev, bits, gs, M, K):
-    """K=384 runs the register-fed GEMV; K=1024 / 2560 (K a multiple of 8 groups) the
-    TMA-fed one, 2560 with a partial last stage."""
+@pytest.mark.parametrize("kernel", [GEMV, GEMV_TMA, GEMV_REGS])
+def test_gemv_parity(dev, bits, gs, M, K, kernel):
+    """The automatic GEMV choice and each mma.sync GEMV pinned: the register-fed one (any
+    K) and the TMA-fed one (K a multiple of 8 groups; 2560 has a partial last stage)."""
+    if kernel == GEMV_TMA and (K // gs) % 8:
+        pytest.skip("the TMA GEMV needs K to be a whole number of 8-group batches")
     N = 200
     _, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 100 * M + gs + bits)
-    y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, kernel=GEMV)
+    y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, kernel=kernel)
     assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(O.quantized_matmul(x, wq, s, b, gs, bits)), what="gemv")
 
 
@@ -156,21 +160,21 @@ def test_gemv_tma_epilogues(dev, bits, epi):
     bias = rand_bf16((N,), 0.2, rng)
     if epi == "bias_gelu":
         y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, bias=np2t(bias, dev), act="gelu_tanh",
-                                     kernel=GEMV)
+                                     kernel=GEMV_TMA)
         ref = O.quantized_matmul(x, wq, s, b, gs, bits, bias=bias, act=O.ACT_GELU_TANH)
         tol = dict(ulps=4, rl2=6e-3)
     elif epi == "swiglu":
         w3 = rand_bf16((N, K), 0.02, rng)
         wq3, s3, b3 = O.quantize(w3, gs, bits)
         y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, act="swiglu",
-                                     up=(np2t(wq3, dev), np2t(s3, dev), np2t(b3, dev)), kernel=GEMV)
+                                     up=(np2t(wq3, dev), np2t(s3, dev), np2t(b3, dev)), kernel=GEMV_TMA)
         ref = O.swiglu(O.quantized_matmul(x, wq, s, b, gs, bits), O.quantized_matmul(x, wq3, s3, b3, gs, bits))
         tol = dict(ulps=4, rl2=6e-3)
     else:
         A = rand_bf16((K, 32), 1.0 / np.sqrt(32), rng)
         B = rand_bf16((32, N), 0.01, rng)
         y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, bias=np2t(bias, dev),
-                                     lora=(np2t(A, dev), np2t(B, dev), 0.5), kernel=GEMV)
+                                     lora=(np2t(A, dev), np2t(B, dev), 0.5), kernel=GEMV_TMA)
         ref = O.quantized_matmul(x, wq, s, b, gs, bits, bias=bias, lora_a=A, lora_b=B, lora_scale=0.5)
         tol = dict(ulps=4, atol_frac=2 ** -7)
     torch.cuda.synchronize()
@@ -240,8 +244,8 @@ def test_gemv_tc_parity(dev, bits, gs, M, K):
     assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(O.quantized_matmul(x, wq, s, b, gs, bits)), what="gemv-tc")
 
 
-@pytest.mark.parametrize("kernel,M", [(GEMV, 1), (GEMV, 5), (GEMV_TC, 3), (GEMM, 300), (GEMM2, 300),
-                                      (GENERIC, 7)])
+@pytest.mark.parametrize("kernel,M", [(GEMV, 1), (GEMV_TMA, 5), (GEMV_REGS, 2), (GEMV_TC, 3), (GEMM, 300),
+                                      (GEMM2, 300), (GENERIC, 7)])
 @pytest.mark.parametrize("gate_mode", ["none", "row", "period"])
 def test_gated_residual_epilogue(dev, kernel, M, gate_mode):
     """y = residual + gate * (x W^T + bias) fused in the epilogue, each op rounded to bf16
