@@ -100,7 +100,6 @@ struct Params {
     const __nv_bfloat16 *lora_b;             // [rank, N]
     int lora_rank;
     __nv_bfloat16 *y;
-    Gated gd;                                // gated residual epilogue
 };
 
 __device__ __forceinline__ float gelu_tanh_f(float x) {
@@ -117,11 +116,13 @@ __device__ __forceinline__ float gelu_erf_f(float x) {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
-template <int BITS, bool SWIGLU, int CG>
-__global__ void __launch_bounds__(NTHREADS, 1)
-    qgemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                 const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_t,
-                 const Params p) {
+// The kernel body.  GATED compiles the gated-residual epilogue in; it is a separate
+// __global__ entry point with its own parameter (qgemm_gated_kernel), so the plain
+// kernel's code and parameter block are exactly those of a kernel without it (a larger
+// Params block measurably slowed the plain kernel).
+template <int BITS, bool SWIGLU, int CG, bool GATED>
+__device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtensorMap &tm_w, const CUtensorMap &tm_w2,
+                                           const CUtensorMap &tm_t, const Params &p, const Gated &gd) {
     using C = Cfg<BITS, CG>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -346,24 +347,44 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                     named_bar_sync(1, 128);
                     if (row < 64 && n < p.N) {
+                        if constexpr (!GATED) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const int m = m0 + c * 32 + i;
-                            const float g = (i & 1) ? bf16hi(pk[i >> 1]) : bf16lo(pk[i >> 1]);
-                            const float u = xch[row * 33 + i];
-                            if (m < p.M)
-                                p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(apply_gated(silu_f(g) * u, p.gd, m, n, p.N));
+                            for (int i = 0; i < 32; ++i) {
+                                const int m = m0 + c * 32 + i;
+                                const float g = (i & 1) ? bf16hi(pk[i >> 1]) : bf16lo(pk[i >> 1]);
+                                const float u = xch[row * 33 + i];
+                                if (m < p.M) p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(silu_f(g) * u);
+                            }
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                const int m = m0 + c * 32 + i;
+                                const float g = (i & 1) ? bf16hi(pk[i >> 1]) : bf16lo(pk[i >> 1]);
+                                const float u = xch[row * 33 + i];
+                                if (m < p.M)
+                                    p.y[(int64_t)m * p.N + n] =
+                                        __float2bfloat16_rn(apply_gated(silu_f(g) * u, gd, m, n, p.N));
+                            }
                         }
                     }
                     named_bar_sync(1, 128);
-                } else if (n < p.N) {
+                } else if (!GATED && n < p.N) {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         const int m = m0 + c * 32 + i;
                         float v = (i & 1) ? bf16hi(pk[i >> 1]) : bf16lo(pk[i >> 1]);
                         if (p.act == QL_ACT_GELU_TANH) v = gelu_tanh_f(v);
                         else if (p.act == QL_ACT_GELU_ERF) v = gelu_erf_f(v);
-                        if (m < p.M) p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(apply_gated(v, p.gd, m, n, p.N));
+                        if (m < p.M) p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(v);
+                    }
+                } else if (GATED && n < p.N) {  // gated residual
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int m = m0 + c * 32 + i;
+                        float v = (i & 1) ? bf16hi(pk[i >> 1]) : bf16lo(pk[i >> 1]);
+                        if (p.act == QL_ACT_GELU_TANH) v = gelu_tanh_f(v);
+                        else if (p.act == QL_ACT_GELU_ERF) v = gelu_erf_f(v);
+                        if (m < p.M) p.y[(int64_t)m * p.N + n] = __float2bfloat16_rn(apply_gated(v, gd, m, n, p.N));
                     }
                 }
             }
@@ -524,6 +545,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
+template <int BITS, bool SWIGLU, int CG>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    qgemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                 const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_t,
+                 const Params p) {
+    qgemm_body<BITS, SWIGLU, CG, false>(tm_x, tm_w, tm_w2, tm_t, p, Gated{});
+}
+
+template <int BITS, bool SWIGLU, int CG>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    qgemm_gated_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                       const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_t,
+                       const Params p, const Gated gd) {
+    qgemm_body<BITS, SWIGLU, CG, true>(tm_x, tm_w, tm_w2, tm_t, p, gd);
+}
+
 // ------------------------------------------------------------------ host side
 
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -560,11 +597,11 @@ static int make_map_2d(CUtensorMap *map, CUtensorMapDataType dt, int elem_bytes,
     return QL_OK;
 }
 
-template <int BITS, bool SWIGLU, int CG>
+template <int BITS, bool SWIGLU, int CG, bool GATED>
 static int launch_t(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mw2,
-                    const CUtensorMap &mt, const Params &p, int max_ctas, cudaStream_t st) {
+                    const CUtensorMap &mt, const Params &p, const Gated &gd, int max_ctas, cudaStream_t st) {
     using C = Cfg<BITS, CG>;
-    auto kfn = qgemm_kernel<BITS, SWIGLU, CG>;
+    auto kfn = GATED ? (const void *)qgemm_gated_kernel<BITS, SWIGLU, CG> : (const void *)qgemm_kernel<BITS, SWIGLU, CG>;
     static bool configured = false;  // per template instance; attribute is per-function
     if (!configured) {
         QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_TOTAL));
@@ -599,7 +636,10 @@ static int launch_t(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensor
     int clusters = tiles < max_clusters ? tiles : max_clusters;
     if (max_ctas > 0 && clusters > max_ctas / CG) clusters = max_ctas / CG > 0 ? max_ctas / CG : 1;
     cfg.gridDim = dim3((unsigned)(clusters * CG));
-    QL_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, mx, mw, mw2, mt, p));
+    if constexpr (GATED)
+        QL_CUDA_TRY(cudaLaunchKernelEx(&cfg, qgemm_gated_kernel<BITS, SWIGLU, CG>, mx, mw, mw2, mt, p, gd));
+    else
+        QL_CUDA_TRY(cudaLaunchKernelEx(&cfg, qgemm_kernel<BITS, SWIGLU, CG>, mx, mw, mw2, mt, p));
     return QL_OK;
 }
 
@@ -613,6 +653,13 @@ extern "C" int ql_debug_trace(unsigned long long *out, int) {
 
 // x [M,K] bf16, W packed [N,K] (+ W3 for SwiGLU), scales/biases bf16.
 // lora_t: [M, r_pad] bf16 (r_pad = round_up(rank, 64)) already holding s.(x.A), or null.
+template <int BITS, bool SWIGLU, int CG>
+static int launch_g(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mw2, const CUtensorMap &mt,
+                    const gemm::Params &p, const Gated &gd, int max_ctas, cudaStream_t st) {
+    return gd.res ? gemm::launch_t<BITS, SWIGLU, CG, true>(mx, mw, mw2, mt, p, gd, max_ctas, st)
+                  : gemm::launch_t<BITS, SWIGLU, CG, false>(mx, mw, mw2, mt, p, gd, max_ctas, st);
+}
+
 int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales,
                        const void *biases, const uint32_t *wq2, const void *scales2,
                        const void *biases2, int64_t N, int gs, int bits, const void *bias,
@@ -622,7 +669,6 @@ int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, 
     const bool swiglu = act == QL_ACT_SWIGLU;
     const int wrows = (swiglu ? 64 : BW) * cg;  // output columns per tile
     Params p{};
-    p.gd = gd;
     p.M = (int)M;
     p.N = (int)N;
     p.K = (int)K;
@@ -669,12 +715,12 @@ int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, 
     }
     if (cg == 2) {
         if (bits == 4)
-            return swiglu ? launch_t<4, true, 2>(mx, mw, mw2, mt, p, max_ctas, st) : launch_t<4, false, 2>(mx, mw, mw2, mt, p, max_ctas, st);
-        return swiglu ? launch_t<8, true, 2>(mx, mw, mw2, mt, p, max_ctas, st) : launch_t<8, false, 2>(mx, mw, mw2, mt, p, max_ctas, st);
+            return swiglu ? launch_g<4, true, 2>(mx, mw, mw2, mt, p, gd, max_ctas, st) : launch_g<4, false, 2>(mx, mw, mw2, mt, p, gd, max_ctas, st);
+        return swiglu ? launch_g<8, true, 2>(mx, mw, mw2, mt, p, gd, max_ctas, st) : launch_g<8, false, 2>(mx, mw, mw2, mt, p, gd, max_ctas, st);
     }
     if (bits == 4)
-        return swiglu ? launch_t<4, true, 1>(mx, mw, mw2, mt, p, max_ctas, st) : launch_t<4, false, 1>(mx, mw, mw2, mt, p, max_ctas, st);
-    return swiglu ? launch_t<8, true, 1>(mx, mw, mw2, mt, p, max_ctas, st) : launch_t<8, false, 1>(mx, mw, mw2, mt, p, max_ctas, st);
+        return swiglu ? launch_g<4, true, 1>(mx, mw, mw2, mt, p, gd, max_ctas, st) : launch_g<4, false, 1>(mx, mw, mw2, mt, p, gd, max_ctas, st);
+    return swiglu ? launch_g<8, true, 1>(mx, mw, mw2, mt, p, gd, max_ctas, st) : launch_g<8, false, 1>(mx, mw, mw2, mt, p, gd, max_ctas, st);
 }
 
 }  // namespace ql
