@@ -142,7 +142,7 @@ def run_reference(args):
     Ms = 32  # bounded sample: 32 of the 4608 tokens per step
     rng = np.random.default_rng(0)
     lin = []
-    for name, N, K, act, _ in flux_linears(cfg):
+    for name, N, K, act, _, _ in flux_linears(cfg):
         w = O.to_bf16((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
         wq, s, b = O.quantize(w, cfg["gs"], cfg["bits"])
         lin.append((name, wq, s, b, O.to_bf16((rng.standard_normal(N) * 0.02).astype(np.float32))))
@@ -188,7 +188,7 @@ def cpu_baseline_sample(cfg):
     rng = np.random.default_rng(1)
     threads = os.cpu_count() or 1
     t_total, flops = 0.0, 0.0
-    for name, N, K, act, _ in flux_linears(cfg):
+    for name, N, K, act, _, _ in flux_linears(cfg):
         w = O.to_bf16((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
         wq, s, b = O.quantize(w, cfg["gs"], cfg["bits"])
         x = O.to_bf16(rng.standard_normal((Ms, K)).astype(np.float32))
