@@ -594,7 +594,7 @@ def run_ours(args):
             result["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                                   "frac": achieved / peak, "peak_kind": f"{src} bf16 sustained",
                                   "frac_of_burst": achieved / peaks["bf16_tflops"],
-                                  "traffic": 175331072, "traffic_launch": "up (ncu dram read+write, profiles/qgemm_flux_up_q8_traffic.md; algorithmic 180.4 MB)",
+                                  "traffic": 180569344, "traffic_launch": "up (ncu dram read+write, profiles/qgemm_flux_up_q8_traffic.md; algorithmic 180.4 MB)",
                                   "kernel": "qgemm_sm100 (4 launches/step, mean ms each)",
                                   "per_launch_ms": {k: statistics.mean(v) for k, v in per.items()}}
     # e2e through the public API with host buffers.  N > 1: every rank moves 1/N of the rows
