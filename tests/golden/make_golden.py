@@ -17,7 +17,9 @@ from safetensors.numpy import load_file
 
 
 def main() -> None:
-    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("QL_REFERENCE", "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("QL_REFERENCE")
+    if not ref:
+        sys.exit("usage: python tests/golden/make_golden.py path/to/reference (or set QL_REFERENCE)")
     src = os.path.join(ref, "tests", "fixtures", "quant_q4q8.safetensors")
     t = load_file(src)
     out = os.path.join(os.path.dirname(os.path.abspath(__file__)), "quant_q4q8.npz")
