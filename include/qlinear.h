@@ -96,6 +96,12 @@ typedef struct {
     const void *residual;      /* [M, N]                                               */
     const void *gate;          /* [M / gate_period, N] or [N]                          */
     int64_t gate_period;       /* token rows per gate row (0: one gate row)            */
+    /* LoKr residual (src/adapters.rs:263-266): y += lokr_scale * x . delta^T, delta a dense
+       [N, K] matrix in x's dtype (the reconstructed Kronecker product).  The tensor-core
+       path adds lokr_scale * delta to each dequantized weight (no extra MMA); it needs
+       the 1-CTA GEMM without SwiGLU (QL_KERNEL_AUTO picks it for any M).  NULL: off.  */
+    const void *lokr_delta;
+    float lokr_scale;
 } ql_epilogue;
 
 /* Library version (major*10000 + minor*100 + patch). */

@@ -43,11 +43,11 @@ int launch_qgemv_tc(const void *, int64_t, int64_t, const uint32_t *, const void
 int launch_qgemm_sm100(const void *, int64_t, int64_t, const uint32_t *, const void *, const void *,
                        const uint32_t *, const void *, const void *, int64_t, int, int, const void *,
                        const void *, int, const void *, const void *, int64_t, void *, int, int, const Gated &,
-                       cudaStream_t);
+                       const void *, float, cudaStream_t);
 int launch_qmm_generic(const void *, int, int64_t, int64_t, const uint32_t *, const void *,
                        const void *, const uint32_t *, const void *, const void *, int, int64_t, int,
                        int, const void *, const void *, int, const void *, const void *, int64_t,
-                       float, void *, int, const Gated &, cudaStream_t);
+                       float, void *, int, const Gated &, const void *, float, cudaStream_t);
 int launch_lora_t(const void *, int64_t, int64_t, const void *, int64_t, float, void *, cudaStream_t);
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -173,7 +173,13 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
     if (e.gate_period < 0) return fail(QL_EINVAL_ARG, "gate_period must be >= 0");
     const Gated gd{e.residual, e.gate, e.gate_period};
     int kernel = e.kernel;
-    if (kernel == QL_KERNEL_AUTO) kernel = !tc_dtypes ? QL_KERNEL_GENERIC : (M <= 8 ? QL_KERNEL_GEMV : QL_KERNEL_GEMM);
+    const bool lokr = e.lokr_delta != nullptr;
+    if (lokr && swiglu) return fail(QL_EUNSUPPORTED, "a LoKr delta cannot be fused with SwiGLU");
+    if (lokr && !aligned16(e.lokr_delta)) return fail(QL_EINVAL_ARG, "lokr_delta must be 16-byte aligned");
+    if (kernel == QL_KERNEL_AUTO)
+        kernel = !tc_dtypes ? QL_KERNEL_GENERIC : ((M <= 8 && !lokr) ? QL_KERNEL_GEMV : QL_KERNEL_GEMM);
+    if (lokr && kernel != QL_KERNEL_GEMM && kernel != QL_KERNEL_GENERIC)
+        return fail(QL_EUNSUPPORTED, "a LoKr delta runs on the 1-CTA GEMM or the generic kernel");
     if (kernel != QL_KERNEL_GENERIC && !tc_dtypes)
         return fail(QL_EUNSUPPORTED, "tensor-core kernels need bf16 x, scales and y");
     if ((kernel == QL_KERNEL_GEMV || kernel == QL_KERNEL_GEMV_TC || kernel == QL_KERNEL_GEMV_TMA ||
@@ -192,7 +198,7 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
         return launch_qmm_generic(x, x_dtype, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up,
                                   sb_dtype, N, group_size, bits, e.bias, e.bias_up, e.act,
                                   lora ? e.lora_a : nullptr, e.lora_b, lora ? e.lora_rank : 0,
-                                  e.lora_scale, y, y_dtype, gd, st);
+                                  e.lora_scale, y, y_dtype, gd, e.lokr_delta, e.lokr_scale, st);
 
     const void *lora_t = nullptr;
     if (lora) {
@@ -209,7 +215,7 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
                             kernel == QL_KERNEL_GEMV_TMA ? 1 : kernel == QL_KERNEL_GEMV_REGS ? 2 : 0, st);
     return launch_qgemm_sm100(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size,
                               bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y,
-                              kernel == QL_KERNEL_GEMM_PAIR ? 2 : 1, e.max_ctas, gd, st);
+                              kernel == QL_KERNEL_GEMM_PAIR ? 2 : 1, e.max_ctas, gd, e.lokr_delta, e.lokr_scale, st);
 }
 
 }  // extern "C"

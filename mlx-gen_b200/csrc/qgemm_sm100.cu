@@ -68,9 +68,11 @@ constexpr uint32_t STG_COL = 384;   // bf16 staging of the finished tile (128 co
 // CG = CTAs per MMA: 1 (cta_group::1, 128 x 256 tile per CTA) or 2 (a CTA pair runs
 // cta_group::2 MMAs on a 256 x 256 tile; each CTA holds 128 weight rows in its TMEM and
 // stages 128 of the 256 tokens in its smem, which halves the x traffic per SM).
-template <int BITS, int CG>
+// LOKR: a dense bf16 LoKr delta tile (128 rows x 64 K, 128-byte swizzled) travels with
+// each packed-W stage; three stages leave room for it.
+template <int BITS, int CG, bool LOKR = false>
 struct Cfg {
-    static constexpr int STAGES = CG == 1 ? 5 : (BITS == 4 ? 8 : 7);  // smem ring depth
+    static constexpr int STAGES = LOKR ? 3 : (CG == 1 ? 5 : (BITS == 4 ? 8 : 7));  // smem ring depth
     static constexpr int XROWS = BT / CG;                          // tokens staged per CTA
     static constexpr int X_STAGE_BYTES = XROWS * BK * 2;           // 32 KB / 16 KB
     static constexpr int W_ROW_BYTES = BK * BITS / 8;              // 32 (Q4) / 64 (Q8)
@@ -78,7 +80,9 @@ struct Cfg {
     static constexpr int W_BOX_WORDS = BK * BITS / 32;             // 8 / 16
     static constexpr int SMEM_X = 0;
     static constexpr int SMEM_W = SMEM_X + STAGES * X_STAGE_BYTES;
-    static constexpr int SMEM_XCH = SMEM_W + STAGES * W_STAGE_BYTES;  // swiglu exchange
+    static constexpr int D_STAGE_BYTES = LOKR ? BW * BK * 2 : 0;   // 16 KB
+    static constexpr int SMEM_D = SMEM_W + STAGES * W_STAGE_BYTES;    // LoKr delta tiles (1 KB aligned)
+    static constexpr int SMEM_XCH = SMEM_D + STAGES * D_STAGE_BYTES;  // swiglu exchange
     static constexpr int XCH_BYTES = 64 * 33 * 4;
     static constexpr int SMEM_BAR = SMEM_XCH + XCH_BYTES;
     static constexpr int NBAR = 3 * STAGES + AST + KR + 2;
@@ -120,10 +124,13 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)
 // __global__ entry point with its own parameter (qgemm_gated_kernel), so the plain
 // kernel's code and parameter block are exactly those of a kernel without it (a larger
 // Params block measurably slowed the plain kernel).
-template <int BITS, bool SWIGLU, int CG, bool GATED>
+// LOKR: the dequant warps add lokr_scale * dW (a dense bf16 [N, K] delta staged by TMA with
+// the packed weights) to each dequantized weight, so a LoKr adapter costs no extra MMA.
+template <int BITS, bool SWIGLU, int CG, bool GATED, bool LOKR = false>
 __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtensorMap &tm_w, const CUtensorMap &tm_w2,
-                                           const CUtensorMap &tm_t, const Params &p, const Gated &gd) {
-    using C = Cfg<BITS, CG>;
+                                           const CUtensorMap &tm_t, const Params &p, const Gated &gd,
+                                           const CUtensorMap *tm_d = nullptr, uint32_t lokr_scale2 = 0) {
+    using C = Cfg<BITS, CG, LOKR>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -220,7 +227,10 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
 #endif
                     // packed W rows of this CTA: counted on the local wfull[s]
                     if (wstep) {
-                        mbar_arrive_expect_tx(&wfull[s], C::W_STAGE_BYTES);
+                        mbar_arrive_expect_tx(&wfull[s], C::W_STAGE_BYTES + C::D_STAGE_BYTES);
+                        if constexpr (LOKR)
+                            tma_load_2d(smem + C::SMEM_D + s * C::D_STAGE_BYTES, tm_d, &wfull[s], kt * BK,
+                                        (wt * CG + (int)rank) * BW);
                         if (SWIGLU) {
                             const int r0 = (wt * CG + (int)rank) * 64;
                             tma_load_2d(ws, &tm_w, &wfull[s], kt * C::W_BOX_WORDS, r0);
@@ -509,6 +519,19 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                     r[c] = lo | (hi << 16);
                 }
             }
+            if constexpr (LOKR) {
+                if (kt < p.ktw) {  // w += scale * dW, one bf16 fma per pair (row's 128 B, swizzled)
+                    const uint8_t *drow = smem + C::SMEM_D + s * C::D_STAGE_BYTES + row * 128;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const uint4 dv = *reinterpret_cast<const uint4 *>(drow + ((c ^ (row & 7)) << 4));
+                        r[4 * c + 0] = hfma2_bf16(dv.x, lokr_scale2, r[4 * c + 0]);
+                        r[4 * c + 1] = hfma2_bf16(dv.y, lokr_scale2, r[4 * c + 1]);
+                        r[4 * c + 2] = hfma2_bf16(dv.z, lokr_scale2, r[4 * c + 2]);
+                        r[4 * c + 3] = hfma2_bf16(dv.w, lokr_scale2, r[4 * c + 3]);
+                    }
+                }
+            }
 #ifndef QL_EXP_NOWST
             tmem_st32(taddr_lane + j * 32, r);
             tmem_st_wait();
@@ -551,6 +574,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                  const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_t,
                  const Params p) {
     qgemm_body<BITS, SWIGLU, CG, false>(tm_x, tm_w, tm_w2, tm_t, p, Gated{});
+}
+
+// Plain or gated linear plus a LoKr delta (1-CTA tiles, no SwiGLU).
+struct LokrArgs {
+    uint32_t scale2;  // lokr_scale as a bf16 pair
+    Gated gd;
+};
+template <int BITS, bool GATED>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    qgemm_lokr_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                      const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_t,
+                      const Params p, const __grid_constant__ CUtensorMap tm_d, const LokrArgs la) {
+    qgemm_body<BITS, false, 1, GATED, true>(tm_x, tm_w, tm_w2, tm_t, p, la.gd, &tm_d, la.scale2);
 }
 
 template <int BITS, bool SWIGLU, int CG>
@@ -643,6 +679,31 @@ static int launch_t(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensor
     return QL_OK;
 }
 
+template <int BITS, bool GATED>
+static int launch_lokr(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mt, const Params &p,
+                       const CUtensorMap &md, const LokrArgs &la, int max_ctas, cudaStream_t st) {
+    using C = Cfg<BITS, 1, true>;
+    auto kfn = qgemm_lokr_kernel<BITS, GATED>;
+    static bool configured = false;
+    if (!configured) {
+        QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_TOTAL));
+        configured = true;
+    }
+    int dev = 0, sms = 148;
+    QL_CUDA_TRY(cudaGetDevice(&dev));
+    QL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int tiles = p.num_w_tiles * p.num_t_tiles;
+    int ctas = tiles < sms ? tiles : sms;
+    if (max_ctas > 0 && ctas > max_ctas) ctas = max_ctas;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ctas);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = C::SMEM_TOTAL;
+    cfg.stream = st;
+    QL_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, mx, mw, mw, mt, p, md, la));
+    return QL_OK;
+}
+
 }  // namespace gemm
 
 #ifdef QL_TRACE
@@ -653,6 +714,14 @@ extern "C" int ql_debug_trace(unsigned long long *out, int) {
 
 // x [M,K] bf16, W packed [N,K] (+ W3 for SwiGLU), scales/biases bf16.
 // lora_t: [M, r_pad] bf16 (r_pad = round_up(rank, 64)) already holding s.(x.A), or null.
+// a float as a pair of bf16 (round to nearest even), host side
+static uint32_t pack_scale_bf16x2(float v) {
+    uint32_t u;
+    memcpy(&u, &v, 4);
+    const uint32_t r = (u + 0x7fffu + ((u >> 16) & 1u)) >> 16;
+    return r | (r << 16);
+}
+
 template <int BITS, bool SWIGLU, int CG>
 static int launch_g(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mw2, const CUtensorMap &mt,
                     const gemm::Params &p, const Gated &gd, int max_ctas, cudaStream_t st) {
@@ -664,7 +733,8 @@ int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, 
                        const void *biases, const uint32_t *wq2, const void *scales2,
                        const void *biases2, int64_t N, int gs, int bits, const void *bias,
                        const void *bias2, int act, const void *lora_t, const void *lora_b,
-                       int64_t rank, void *y, int cg, int max_ctas, const Gated &gd, cudaStream_t st) {
+                       int64_t rank, void *y, int cg, int max_ctas, const Gated &gd, const void *lokr_delta,
+                       float lokr_scale, cudaStream_t st) {
     using namespace gemm;
     const bool swiglu = act == QL_ACT_SWIGLU;
     const int wrows = (swiglu ? 64 : BW) * cg;  // output columns per tile
@@ -712,6 +782,19 @@ int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, 
         rc = make_map_2d(&mt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, lora_t, (uint64_t)rpad, (uint64_t)M,
                          (uint64_t)rpad * 2, BK, xbox, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
+    }
+    if (lokr_delta) {  // LoKr delta fused into the dequant (1-CTA tiles, no SwiGLU)
+        if (swiglu || cg != 1) return fail(QL_EUNSUPPORTED, "a fused LoKr delta needs the 1-CTA GEMM without SwiGLU");
+        CUtensorMap md;
+        rc = make_map_2d(&md, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, lokr_delta, (uint64_t)K, (uint64_t)N,
+                         (uint64_t)K * 2, BK, BW, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+        LokrArgs la{pack_scale_bf16x2(lokr_scale), gd};
+        if (bits == 4)
+            return gd.res ? launch_lokr<4, true>(mx, mw, mt, p, md, la, max_ctas, st)
+                          : launch_lokr<4, false>(mx, mw, mt, p, md, la, max_ctas, st);
+        return gd.res ? launch_lokr<8, true>(mx, mw, mt, p, md, la, max_ctas, st)
+                      : launch_lokr<8, false>(mx, mw, mt, p, md, la, max_ctas, st);
     }
     if (cg == 2) {
         if (bits == 4)

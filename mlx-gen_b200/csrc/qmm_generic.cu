@@ -36,6 +36,8 @@ struct Params {
     void *y;
     int ydt;
     Gated gd;  // residual and gate in y's dtype
+    const void *lokr_delta;  // [N, K] in x's dtype, or null
+    float lokr_scale;
 };
 
 __device__ __forceinline__ float act_f(float v, int act) {
@@ -70,6 +72,8 @@ __global__ void __launch_bounds__(256) qmm_generic_kernel(const Params p) {
                     const int64_t g = (int64_t)n * p.G + k / p.gs;
                     v = round_to(p.sdt, fmaf((float)code, load_as_f32(p.scales[ps], p.sdt, g),
                                              load_as_f32(p.biases[ps], p.sdt, g)));
+                    if (p.lokr_delta && ps == 0)  // LoKr: w + scale * delta, in fp32
+                        v = fmaf(p.lokr_scale, load_as_f32(p.lokr_delta, p.xdt, (int64_t)n * p.K + k), v);
                 }
                 ws[ps][r][kk] = v;
             }
@@ -280,9 +284,11 @@ int launch_qmm_generic(const void *x, int xdt, int64_t M, int64_t K, const uint3
                        const void *scales2, const void *biases2, int sdt, int64_t N, int gs,
                        int bits, const void *bias, const void *bias2, int act, const void *lora_a,
                        const void *lora_b, int64_t rank, float lora_scale, void *y, int ydt,
-                       const Gated &gd, cudaStream_t st) {
+                       const Gated &gd, const void *lokr_delta, float lokr_scale, cudaStream_t st) {
     generic::Params p{};
     p.gd = gd;
+    p.lokr_delta = lokr_delta;
+    p.lokr_scale = lokr_scale;
     p.x = x;
     p.xdt = xdt;
     p.M = (int)M;

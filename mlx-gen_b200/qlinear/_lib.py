@@ -72,6 +72,8 @@ class Epilogue(C.Structure):
         ("residual", C.c_void_p),
         ("gate", C.c_void_p),
         ("gate_period", C.c_int64),
+        ("lokr_delta", C.c_void_p),
+        ("lokr_scale", C.c_float),
     ]
 
 

@@ -65,12 +65,12 @@ class QuantizedLinear:
 
     def forward(self, x: torch.Tensor, *, act: Optional[str] = None, lora=None,
                 kernel: int = KERNEL_AUTO, residual: Optional[torch.Tensor] = None,
-                gate: Optional[torch.Tensor] = None, gate_period: int = 0) -> torch.Tensor:
+                gate: Optional[torch.Tensor] = None, gate_period: int = 0, lokr=None) -> torch.Tensor:
         """``residual``/``gate`` fuse the DiT blocks' gated residual ``residual + gate * y``
         (the reference's ``nn::gated``, src/nn.rs:166-176) into the epilogue."""
         return ops.quantized_matmul(x, self.weight, self.scales, self.biases, True, self.group_size,
                                     self.bits, bias=self.bias, act=act, lora=lora, kernel=kernel,
-                                    residual=residual, gate=gate, gate_period=gate_period)
+                                    residual=residual, gate=gate, gate_period=gate_period, lokr=lokr)
 
 
 @dataclass
@@ -167,14 +167,18 @@ class AdaptableLinear:
 
     # ---- forward (src/adapters.rs:543-549)
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """``base(x) + sum residual(x)``.  A quantized base with exactly one LoRA adapter and
-        bf16 activations runs as ONE fused kernel (the residual accumulates into the same
-        fp32 tile before rounding); any other stack adds the residuals separately."""
-        if (isinstance(self.base, QuantizedLinear) and len(self.adapters) == 1
-                and isinstance(self.adapters[0], Lora) and x.dtype == torch.bfloat16
-                and self.base.scales.dtype == torch.bfloat16):
-            ad = self.adapters[0]
-            return self.base.forward(x, lora=(ad.a, ad.b, ad.scale))
+        """``base(x) + sum residual(x)``.  A quantized base with bf16 activations and at
+        most one LoRA plus at most one LoKr adapter runs as ONE fused kernel (the LoRA
+        residual accumulates into the same fp32 tile, the LoKr delta is added to the
+        dequantized weights); any other stack adds the residuals separately."""
+        loras = [a for a in self.adapters if isinstance(a, Lora)]
+        lokrs = [a for a in self.adapters if isinstance(a, Lokr)]
+        if (isinstance(self.base, QuantizedLinear) and x.dtype == torch.bfloat16
+                and self.base.scales.dtype == torch.bfloat16 and self.adapters
+                and len(loras) <= 1 and len(lokrs) <= 1):
+            lo = (loras[0].a, loras[0].b, loras[0].scale) if loras else None
+            lk = (lokrs[0].delta, lokrs[0].scale) if lokrs else None
+            return self.base.forward(x, lora=lo, lokr=lk)
         out = self.base.forward(x)
         for ad in self.adapters:
             out = out + ad.residual(x)

@@ -104,7 +104,8 @@ def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, bi
                      lora: Optional[tuple] = None, workspace: Optional[torch.Tensor] = None,
                      kernel: int = KERNEL_AUTO, out: Optional[torch.Tensor] = None,
                      max_ctas: int = 0, residual: Optional[torch.Tensor] = None,
-                     gate: Optional[torch.Tensor] = None, gate_period: int = 0) -> torch.Tensor:
+                     gate: Optional[torch.Tensor] = None, gate_period: int = 0,
+                     lokr: Optional[tuple] = None) -> torch.Tensor:
     """``y = x . dequant(W)^T`` (+ fused epilogue), like ``mlx_rs::ops::quantized_matmul``
     with ``transpose=true`` followed by the ops the reference runs after it.
 
@@ -112,7 +113,8 @@ def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, bi
     src/adapters.rs:318-320 does).  act: None, "gelu_tanh", "gelu" or "swiglu" (then
     ``up = (wq3, scales3, biases3[, bias3])`` is the second projection and the result is
     ``silu(x W^T) * (x W3^T)``).  lora: ``(A [K, r], B [r, N], scale)`` adds
-    ``scale * (x.A).B``.  residual / gate: the gated residual ``residual + gate * y``
+    ``scale * (x.A).B``.  lokr: ``(delta [N, K], scale)`` adds ``scale * x.delta^T``
+    (src/adapters.rs:263-266), fused into the dequantized weights.  residual / gate: the gated residual ``residual + gate * y``
     (src/nn.rs:166-176), gate ``[N]`` or ``[M / gate_period, N]``.  Output dtype = x's
     dtype."""
     _need_cuda(x, wq, scales, biases, bias)
@@ -155,6 +157,14 @@ def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, bi
         keep.append(workspace)
         ep.workspace = workspace.data_ptr()
         ep.workspace_bytes = workspace.numel() * workspace.element_size()
+    if lokr is not None:
+        delta, lscale = lokr
+        delta = delta.to(x.dtype).contiguous()
+        if tuple(delta.shape) != (N, K):
+            raise ValueError(f"LoKr delta must be [{N}, {K}], got {tuple(delta.shape)}")
+        keep.append(delta)
+        ep.lokr_delta = delta.data_ptr()
+        ep.lokr_scale = float(lscale)
     if residual is not None:
         residual = residual.to(y.dtype).reshape(-1, N).contiguous()
         keep.append(residual)

@@ -175,3 +175,19 @@ def gated(res, gate, y, period=0):
         y32 = bf16_to_f32(to_bf16(g[rows] * y32))
     return to_bf16(bf16_to_f32(np.ascontiguousarray(res)) + y32)
 
+
+def lokr_residual(x, delta, scale):
+    """``scale * x . delta^T`` as the reference computes it for bf16 x: delta cast to x's
+    dtype, the matmul rounded to bf16, then the scalar product rounded
+    (src/adapters.rs:263-266).  bf16 bits in and out."""
+    xm = bf16_to_f32(np.ascontiguousarray(x)).astype(np.float64)
+    dm = bf16_to_f32(np.ascontiguousarray(delta)).astype(np.float64)
+    r = bf16_to_f32(to_bf16((xm @ dm.T).astype(np.float32)))
+    s = bf16_to_f32(to_bf16(np.float32([scale])))[0]
+    return to_bf16(r * s)
+
+
+def add_bf16(a, b):
+    """Elementwise bf16 add, rounded (the residual sum of AdaptableLinear::forward)."""
+    return to_bf16(bf16_to_f32(np.ascontiguousarray(a)) + bf16_to_f32(np.ascontiguousarray(b)))
+

@@ -270,3 +270,42 @@ def test_gated_residual_epilogue(dev, kernel, M, gate_mode):
     ref = O.gated(res, gate, lin, period)
     # the linear's own tolerance, carried through the gate (|gate| ~ 1) and the residual add
     assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), ulps=4, what=f"gated {gate_mode}")
+
+
+@pytest.mark.parametrize("kernel,M", [(qlinear.KERNEL_AUTO, 3), (GEMM, 300), (GENERIC, 9)])
+@pytest.mark.parametrize("bits", [4, 8])
+def test_lokr_delta(dev, kernel, M, bits):
+    """LoKr residual ``scale * x . delta^T`` (dense delta, src/adapters.rs:263-266) fused
+    into the dequantized weights, against the reference's separate rounding of base and
+    residual (4 ulps + 1/128 of the output scale, as for LoRA); M <= 8 on AUTO runs the
+    GEMM (the GEMV kernels do not take a delta)."""
+    N, K, gs = 256, 1024, 64
+    rng, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 61 + M + bits)
+    bias = rand_bf16((N,), 0.2, rng)
+    delta = rand_bf16((N, K), 0.01, rng)
+    scale = 0.75
+    y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, bias=np2t(bias, dev),
+                                 lokr=(np2t(delta, dev), scale), kernel=kernel)
+    torch.cuda.synchronize()
+    assert qlinear.device_error() == 0
+    ref = O.add_bf16(O.quantized_matmul(x, wq, s, b, gs, bits, bias=bias), O.lokr_residual(x, delta, scale))
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), ulps=4, atol_frac=2 ** -7, what="lokr")
+
+
+def test_lokr_with_lora_and_gate_through_adaptable_linear(dev):
+    """AdaptableLinear with one LoRA and one LoKr adapter runs fused (one call), with the
+    gated residual on top, against the reference's op-by-op composition."""
+    M, N, K, gs, bits = 260, 384, 512, 64, 4
+    rng, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 77)
+    A = rand_bf16((K, 16), 1.0 / 4, rng)
+    B = rand_bf16((16, N), 0.01, rng)
+    delta = rand_bf16((N, K), 0.01, rng)
+    lin = qlinear.AdaptableLinear.from_quantized_parts(wqt, st, bt, None, gs, bits)
+    lin.push(qlinear.Lora(np2t(A, dev), np2t(B, dev), 0.5))
+    lin.push(qlinear.Lokr(np2t(delta, dev), 2.0))
+    y = lin.forward(xt)
+    torch.cuda.synchronize()
+    assert qlinear.device_error() == 0
+    base = O.quantized_matmul(x, wq, s, b, gs, bits, lora_a=A, lora_b=B, lora_scale=0.5)
+    ref = O.add_bf16(base, O.lokr_residual(x, delta, 2.0))
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), ulps=4, atol_frac=2 ** -7, what="lora+lokr")
