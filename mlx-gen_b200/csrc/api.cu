@@ -49,6 +49,8 @@ int launch_qmm_generic(const void *, int, int64_t, int64_t, const uint32_t *, co
                        int, const void *, const void *, int, const void *, const void *, int64_t,
                        float, void *, int, const Gated &, const void *, float, cudaStream_t);
 int launch_lora_t(const void *, int64_t, int64_t, const void *, int64_t, float, void *, cudaStream_t);
+int launch_ln_modulate(const void *, int64_t, int64_t, float, const void *, const void *, int64_t, void *, int,
+                       cudaStream_t);
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 static bool valid_dtype(int dt) { return dt == QL_F32 || dt == QL_BF16 || dt == QL_F16; }
@@ -115,6 +117,18 @@ int ql_dequantize(const uint32_t *wq, const void *scales, const void *biases, in
         return fail(QL_EINVAL_ARG, "ql_dequantize: wq and out must be 16-byte aligned");
     return launch_dequantize(nullptr, N, N, K, group_size, bits, wq, scales, biases, sb_dtype, out,
                              out_dtype, (cudaStream_t)stream);
+}
+
+int ql_layernorm_modulate(const void *x, int64_t M, int64_t D, float eps, const void *scale, const void *shift,
+                          int64_t period, void *y, int y_dtype, void *stream) {
+    g_err[0] = 0;
+    if (M < 0 || D <= 0 || D % 8) return fail(QL_EINVAL_SHAPE, "ql_layernorm_modulate: D must be a positive multiple of 8");
+    if (M == 0) return QL_OK;
+    if (!x || !y) return fail(QL_EINVAL_ARG, "ql_layernorm_modulate: NULL pointer");
+    if (y_dtype != QL_BF16 && y_dtype != QL_F32) return fail(QL_EUNSUPPORTED, "y must be bf16 or f32");
+    if (period < 0) return fail(QL_EINVAL_ARG, "period must be >= 0");
+    if (!aligned16(x) || !aligned16(y)) return fail(QL_EINVAL_ARG, "x and y must be 16-byte aligned");
+    return launch_ln_modulate(x, M, D, eps, scale, shift, period, y, y_dtype, (cudaStream_t)stream);
 }
 
 int ql_dequantize_rows(const int64_t *ids, int64_t R, const uint32_t *wq, const void *scales,

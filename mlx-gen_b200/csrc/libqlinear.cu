@@ -11,3 +11,4 @@
 #include "qmm_generic.cu"
 #include "quantize.cu"
 #include "noalloc.cu"
+#include "modulate.cu"

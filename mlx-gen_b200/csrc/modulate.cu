@@ -1,0 +1,100 @@
+// modulate.cu -- the adaLN prologue of the DiT linears in one pass:
+//     y = (1 + scale) * layer_norm(x) + shift
+// as FLUX's blocks compute it before their QKV / MLP linears
+// (mlx-gen-flux/src/transformer.rs:891-913 -> mlx_rs::fast::layer_norm(x, None, None, eps)
+// and src/nn.rs:262-287 `modulate`).  HBM-bound: one read of x, one write of y.
+//
+// Rounding follows the reference's op sequence on bf16 arrays: the normalisation is
+// computed in fp32 (mean, then the variance of x - mean) and rounded to bf16; with a bf16
+// output (FLUX.1: the literal 1 cast to scale's dtype) 1 + scale, the product and the sum
+// are each rounded to bf16; with an f32 output (FLUX.2: a strong f32 1) they are f32.
+// scale / shift: [rows, D] with row m / period (period 0: one row for every m), or NULL
+// (plain layer norm).
+#include "ql_common.cuh"
+
+namespace ql {
+namespace modulate_k {
+
+constexpr int THREADS = 256;
+
+__device__ __forceinline__ float block_sum(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();  // red is reused between calls
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < THREADS / 32; ++w) t += red[w];
+    return t;
+}
+
+// one CTA per row; rows of a few KB stay in L1 between the passes
+template <bool F32_OUT>
+__global__ void __launch_bounds__(THREADS) ln_modulate_kernel(const __nv_bfloat16 *__restrict__ x, int D, float eps,
+                                                              const __nv_bfloat16 *__restrict__ scale,
+                                                              const __nv_bfloat16 *__restrict__ shift, int64_t period,
+                                                              void *__restrict__ y) {
+    __shared__ float red[THREADS / 32];
+    const int64_t m = blockIdx.x;
+    const __nv_bfloat16 *xr = x + m * D;
+    const int D2 = D / 2;  // D is even; bf16 pairs
+    const __nv_bfloat162 *x2 = reinterpret_cast<const __nv_bfloat162 *>(xr);
+    float s = 0.f;
+    for (int i = threadIdx.x; i < D2; i += THREADS) {
+        const float2 v = __bfloat1622float2(x2[i]);
+        s += v.x + v.y;
+    }
+    const float mean = block_sum(s, red) / (float)D;
+    float q = 0.f;
+    for (int i = threadIdx.x; i < D2; i += THREADS) {
+        const float2 v = __bfloat1622float2(x2[i]);
+        const float a = v.x - mean, b = v.y - mean;
+        q += a * a + b * b;
+    }
+    const float var = block_sum(q, red) / (float)D;
+    const float inv = 1.0f / sqrtf(var + eps);
+    const int64_t gr = period > 0 ? m / period : 0;
+    const __nv_bfloat16 *sc = scale ? scale + gr * D : nullptr;
+    const __nv_bfloat16 *sh = shift ? shift + gr * D : nullptr;
+    for (int i = threadIdx.x; i < D2; i += THREADS) {
+        const float2 v = __bfloat1622float2(x2[i]);
+        float n[2] = {round_bf16((v.x - mean) * inv), round_bf16((v.y - mean) * inv)};
+        float o[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int k = 2 * i + h;
+            float r = n[h];
+            if (sc) {
+                const float s1 = __bfloat162float(sc[k]) + 1.0f;
+                r = F32_OUT ? r * s1 : round_bf16(r * round_bf16(s1));
+                if (!F32_OUT) r = round_bf16(r);
+            }
+            if (sh) r = r + __bfloat162float(sh[k]);
+            o[h] = r;
+        }
+        if (F32_OUT)
+            reinterpret_cast<float2 *>(y)[m * D2 + i] = make_float2(o[0], o[1]);
+        else
+            reinterpret_cast<uint32_t *>(y)[m * D2 + i] = pack_bf16x2(o[0], o[1]);
+    }
+}
+
+}  // namespace modulate_k
+
+int launch_ln_modulate(const void *x, int64_t M, int64_t D, float eps, const void *scale, const void *shift,
+                       int64_t period, void *y, int y_dtype, cudaStream_t st) {
+    if (M <= 0) return QL_OK;
+    const dim3 grid((unsigned)M);
+    if (y_dtype == QL_F32)
+        modulate_k::ln_modulate_kernel<true><<<grid, modulate_k::THREADS, 0, st>>>(
+            (const __nv_bfloat16 *)x, (int)D, eps, (const __nv_bfloat16 *)scale, (const __nv_bfloat16 *)shift, period, y);
+    else
+        modulate_k::ln_modulate_kernel<false><<<grid, modulate_k::THREADS, 0, st>>>(
+            (const __nv_bfloat16 *)x, (int)D, eps, (const __nv_bfloat16 *)scale, (const __nv_bfloat16 *)shift, period, y);
+    QL_CUDA_TRY(cudaGetLastError());
+    return QL_OK;
+}
+
+}  // namespace ql

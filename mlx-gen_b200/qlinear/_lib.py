@@ -37,6 +37,7 @@ EXPORTS = (
     "ql_quantize",
     "ql_dequantize",
     "ql_dequantize_rows",
+    "ql_layernorm_modulate",
     "ql_quantized_matmul",
     "ql_matmul_workspace_size",
     "ql_quantized_matmul_noalloc",
@@ -97,12 +98,13 @@ def lib():
         L.ql_quantize.argtypes = [vp, i32, i64, i64, i32, i32, vp, vp, vp, i32, vp]
         L.ql_dequantize.argtypes = [vp, vp, vp, i32, i64, i64, i32, i32, vp, i32, vp]
         L.ql_dequantize_rows.argtypes = [vp, i64, vp, vp, vp, i32, i64, i64, i32, i32, vp, i32, vp]
+        L.ql_layernorm_modulate.argtypes = [vp, i64, i64, C.c_float, vp, vp, i64, vp, i32, vp]
         L.ql_quantized_matmul.argtypes = [vp, i32, i64, i64, vp, vp, vp, i32, i64, i32, i32, i32,
                                           C.POINTER(Epilogue), vp, i32, vp]
         L.ql_quantized_matmul_noalloc.argtypes = L.ql_quantized_matmul.argtypes
         L.ql_matmul_workspace_size.argtypes = [i64, i64, i64, C.POINTER(Epilogue)]
         L.ql_matmul_workspace_size.restype = C.c_size_t
-        for f in ("ql_quantize", "ql_dequantize", "ql_dequantize_rows", "ql_quantized_matmul",
+        for f in ("ql_quantize", "ql_dequantize", "ql_dequantize_rows", "ql_layernorm_modulate", "ql_quantized_matmul",
                   "ql_quantized_matmul_noalloc"):
             getattr(L, f).restype = i32
         _lib = L

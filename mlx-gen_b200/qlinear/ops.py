@@ -89,6 +89,23 @@ def dequantize_rows(ids: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, b
     return out.reshape(*ids.shape, K)
 
 
+def layernorm_modulate(x: torch.Tensor, scale: Optional[torch.Tensor] = None, shift: Optional[torch.Tensor] = None,
+                       eps: float = 1e-6, period: int = 0, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """``(1 + scale) * layer_norm(x) + shift`` in one pass (the DiT adaLN prologue:
+    ``fast::layer_norm`` then ``nn::modulate``, mlx-gen-flux/src/transformer.rs:891-913).
+    x bf16 ``[..., D]``; scale / shift ``[D]`` or ``[rows, D]`` with row ``m // period``.
+    out_dtype bf16: FLUX.1 rounding (every op in bf16); float32: FLUX.2 (a strong f32 1)."""
+    _need_cuda(x, scale, shift)
+    D = x.shape[-1]
+    x2 = x.reshape(-1, D).to(torch.bfloat16).contiguous()
+    y = torch.empty(x2.shape, dtype=out_dtype, device=x.device)
+    sc = None if scale is None else scale.to(torch.bfloat16).reshape(-1, D).contiguous()
+    sh = None if shift is None else shift.to(torch.bfloat16).reshape(-1, D).contiguous()
+    check(lib().ql_layernorm_modulate(_ptr(x2), x2.shape[0], D, float(eps), _ptr(sc), _ptr(sh), int(period),
+                                      _ptr(y), dtype_code(y), _stream(x.device)))
+    return y.reshape(x.shape)
+
+
 def workspace_size(M: int, N: int, K: int, lora_rank: int = 0) -> int:
     ep = Epilogue()
     if lora_rank:

@@ -191,3 +191,29 @@ def add_bf16(a, b):
     """Elementwise bf16 add, rounded (the residual sum of AdaptableLinear::forward)."""
     return to_bf16(bf16_to_f32(np.ascontiguousarray(a)) + bf16_to_f32(np.ascontiguousarray(b)))
 
+
+def layernorm_modulate(x, scale=None, shift=None, eps=1e-6, period=0, f32_out=False):
+    """``(1 + scale) * layer_norm(x) + shift`` with the reference's rounding points:
+    mlx fast::layer_norm (fp32 statistics, output rounded to bf16), then nn::modulate
+    (src/nn.rs:262-287): with one_matches_scale every op rounded to bf16 (FLUX.1), else
+    f32 arithmetic and an f32 result (FLUX.2).  x, scale, shift bf16 bits.  The mean and
+    variance are taken in float64 (the reference's exact fp32 reduction order is not
+    published): rounding ties of the bf16 normalised value may differ."""
+    xf = bf16_to_f32(np.ascontiguousarray(x)).astype(np.float64)
+    M, D = xf.shape
+    mean = xf.mean(axis=1, keepdims=True)
+    var = ((xf - mean) ** 2).mean(axis=1, keepdims=True)
+    n = bf16_to_f32(to_bf16(((xf - mean) / np.sqrt(var + eps)).astype(np.float32)))
+    rows = (np.arange(M) // period) if period > 0 else np.zeros(M, np.int64)
+    r = n
+    if scale is not None:
+        s = bf16_to_f32(np.ascontiguousarray(scale)).reshape(-1, D)[rows]
+        if f32_out:
+            r = (r * (s + np.float32(1.0))).astype(np.float32)
+        else:
+            r = bf16_to_f32(to_bf16(r * bf16_to_f32(to_bf16(s + np.float32(1.0)))))
+    if shift is not None:
+        h = bf16_to_f32(np.ascontiguousarray(shift)).reshape(-1, D)[rows]
+        r = (r + h).astype(np.float32)
+    return r.astype(np.float32) if f32_out else to_bf16(r)
+
