@@ -207,13 +207,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         *abort_flag = 0;
         mbar_fence_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
-    tc_fence_before();
     __syncthreads();
     if (p.split > 1) cluster_sync_all();  // peers' barriers are initialised before any remote arrive
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // the TMEM allocation happens off the producer's path: the weight stream starts now and
+    // the TMEM users pick the address up at the barrier below
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tc_fence_before();
+    }
 #ifdef QL_TRACE
     if (threadIdx.x == 32) {
         g_trace[9][blockIdx.x % 160] -= clock64();
@@ -298,7 +300,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to tcgen05.mma
     }
-    if (warp >= 1) named_bar_sync(1, NTHREADS - 32);  // warps 1-15: pieces and group info ready
+    if (warp >= 1) named_bar_sync(1, NTHREADS - 32);  // warps 1-15: pieces, group info and TMEM ready
+    tc_fence_after();
+    const uint32_t tmem = warp >= 1 ? *tmem_slot : 0u;
 #ifdef QL_TRACE
     if (threadIdx.x == 32) g_trace[12][blockIdx.x % 160] += clock64() - t_entry;
 #endif
