@@ -357,6 +357,18 @@ def other_configs(dev, iters=5):
     return out
 
 
+def slice_bounds(M, chunks, world):
+    """Token-row slices [(r0, r1), ...] for the overlapped reductions: about `chunks` slices,
+    each a multiple of 32 * world rows except possibly the last, and every slice a
+    multiple of `world` rows (a reduce-scatter gives each rank (r1 - r0) / world rows)."""
+    if M % world:
+        raise ValueError("M must be a multiple of the GPU count")
+    unit = 32 * world
+    step = (M + chunks - 1) // chunks
+    step = (step + unit - 1) // unit * unit
+    return [(r0, min(M, r0 + step)) for r0 in range(0, M, step)]
+
+
 class TPBlock:
     """The linears of one DiT block, Megatron-sharded over the ranks (N = 1: unsharded).
 
@@ -399,15 +411,7 @@ class TPBlock:
         # reduce-scattered rows of this rank and the re-gathered full tensor
         self.out = {n: torch.empty(self.M, l["N"], device=dev, dtype=torch.bfloat16) for n, l in self.lin.items()}
         self.row = world > 1
-        if self.row:
-            if self.M % world:
-                raise ValueError("M must be a multiple of the GPU count")
-            unit = 32 * world
-            step = (self.M + chunks - 1) // chunks
-            step = (step + unit - 1) // unit * unit
-            self.bounds = [(r0, min(self.M, r0 + step)) for r0 in range(0, self.M, step)]
-        else:
-            self.bounds = [(0, self.M)]
+        self.bounds = slice_bounds(self.M, chunks, world) if self.row else [(0, self.M)]
         self.mode = mode
         self.shard, self.full = {}, {}
         for n, l in self.lin.items():
