@@ -53,7 +53,10 @@ constexpr int STAGES = 3;     // weight stages of 128 rows x 256 bytes
 constexpr int CPS = 4;        // chunks per stage: 64 packed bytes of a row = 128 K elements
 constexpr int SBR = 4;        // scale/bias ring (batches of 8 groups)
 constexpr int AR = 8;         // A ring: 8 chunks of 32 TMEM columns (columns 0-255)
-constexpr int NISSUE = 3;     // MMA issuer warps
+#ifndef QL_GEMV_NISSUE
+#define QL_GEMV_NISSUE 3
+#endif
+constexpr int NISSUE = QL_GEMV_NISSUE;  // MMA issuer warps (1-3)
 constexpr int NTHREADS = 512; // warps: 0 TMA, 1-3 MMA, 4-7 dequant, 8-15 fold (2 sets)
 constexpr int NCONV = NTHREADS - 64;  // warps 2-15 convert the activations at the start
 constexpr uint32_t TMEM_COLS = 512;
