@@ -132,6 +132,10 @@ int ql_dequantize(const uint32_t *wq, const void *scales, const void *biases, in
  * followed by dequantize and a cast (src/nn.rs:42-59).  ids [R] int64 into the
  * N rows; out [R, K] in out_dtype.  An id outside [0, N) yields a zero row and
  * sets the device error word. */
+int ql_dequantize_rows(const int64_t *ids, int64_t R, const uint32_t *wq, const void *scales,
+                       const void *biases, int sb_dtype, int64_t N, int64_t K, int group_size,
+                       int bits, void *out, int out_dtype, void *stream);
+
 /* The DiT blocks' adaLN prologue in one pass: y = (1 + scale) * layer_norm(x) + shift.
    Replaces mlx_rs::fast::layer_norm(x, None, None, eps) followed by nn::modulate
    (mlx-gen-flux/src/transformer.rs:891-913, src/nn.rs:262-287).  x bf16 [M, D], D a
@@ -140,10 +144,6 @@ int ql_dequantize(const uint32_t *wq, const void *scales, const void *biases, in
    in scale's dtype); QL_F32: computed and stored in f32 (FLUX.2, a strong f32 1). */
 int ql_layernorm_modulate(const void *x, int64_t M, int64_t D, float eps, const void *scale, const void *shift,
                           int64_t period, void *y, int y_dtype, void *stream);
-
-int ql_dequantize_rows(const int64_t *ids, int64_t R, const uint32_t *wq, const void *scales,
-                       const void *biases, int sb_dtype, int64_t N, int64_t K, int group_size,
-                       int bits, void *out, int out_dtype, void *stream);
 
 /* Replaces mlx_rs::ops::quantized_matmul(x, wq, scales, biases, transpose=true,
  * group_size, bits) as called by LinearBase::forward (src/adapters.rs:309-317),
