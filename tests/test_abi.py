@@ -82,6 +82,47 @@ def test_validation_errors_need_no_gpu():
     assert rc == _lib.QL_EINVAL_ARG and b"workspace" in L.ql_last_error()
     # M == 0 is a no-op
     assert L.ql_quantized_matmul(dummy, 1, 0, 128, dummy, dummy, dummy, 1, 64, 64, 4, 1, None, dummy, 1, None) == 0
+    # gated residual: a gate needs a residual, the period is >= 0
+    ep = _lib.Epilogue()
+    ep.gate = 0x1000
+    rc = L.ql_quantized_matmul(dummy, 1, 4, 128, dummy, dummy, dummy, 1, 64, 64, 4, 1, C.byref(ep), dummy, 1, None)
+    assert rc == _lib.QL_EINVAL_ARG and b"residual" in L.ql_last_error()
+    ep.residual = 0x1000
+    ep.gate_period = -1
+    rc = L.ql_quantized_matmul(dummy, 1, 4, 128, dummy, dummy, dummy, 1, 64, 64, 4, 1, C.byref(ep), dummy, 1, None)
+    assert rc == _lib.QL_EINVAL_ARG
+    # LoKr: not with SwiGLU, not on a GEMV kernel, 16-byte aligned
+    ep = _lib.Epilogue()
+    ep.lokr_delta = 0x1000
+    ep.act = _lib.ACT_SWIGLU
+    ep.wq_up = ep.scales_up = ep.biases_up = 0x1000
+    rc = L.ql_quantized_matmul(dummy, 1, 4, 128, dummy, dummy, dummy, 1, 64, 64, 4, 1, C.byref(ep), dummy, 1, None)
+    assert rc == _lib.QL_EUNSUPPORTED
+    ep = _lib.Epilogue()
+    ep.lokr_delta = 0x1000
+    ep.kernel = _lib.KERNEL_GEMV
+    rc = L.ql_quantized_matmul(dummy, 1, 4, 128, dummy, dummy, dummy, 1, 64, 64, 4, 1, C.byref(ep), dummy, 1, None)
+    assert rc == _lib.QL_EUNSUPPORTED and b"LoKr" in L.ql_last_error()
+    ep.kernel = _lib.KERNEL_AUTO
+    ep.lokr_delta = 0x1004
+    rc = L.ql_quantized_matmul(dummy, 1, 4, 128, dummy, dummy, dummy, 1, 64, 64, 4, 1, C.byref(ep), dummy, 1, None)
+    assert rc == _lib.QL_EINVAL_ARG
+    # explicit kernels that cannot take the shape fail instead of falling back
+    ep = _lib.Epilogue()
+    ep.kernel = _lib.KERNEL_GEMV_TMA
+    rc = L.ql_quantized_matmul(dummy, 1, 4, 384, dummy, dummy, dummy, 1, 64, 64, 4, 1, C.byref(ep), dummy, 1, None)
+    assert rc == _lib.QL_EUNSUPPORTED
+    ep.kernel = 8
+    rc = L.ql_quantized_matmul(dummy, 1, 4, 128, dummy, dummy, dummy, 1, 64, 64, 4, 1, C.byref(ep), dummy, 1, None)
+    assert rc == _lib.QL_EINVAL_ARG and b"unknown kernel" in L.ql_last_error()
+    # layer norm + modulate: D a multiple of 8, bf16 or f32 output, aligned pointers
+    rc = L.ql_layernorm_modulate(dummy, 4, 12, 1e-6, None, None, 0, dummy, 1, None)
+    assert rc == _lib.QL_EINVAL_SHAPE
+    rc = L.ql_layernorm_modulate(dummy, 4, 64, 1e-6, None, None, 0, dummy, 2, None)
+    assert rc == _lib.QL_EUNSUPPORTED
+    rc = L.ql_layernorm_modulate(dummy, 4, 64, 1e-6, None, None, -1, dummy, 1, None)
+    assert rc == _lib.QL_EINVAL_ARG
+    assert L.ql_layernorm_modulate(dummy, 0, 64, 1e-6, None, None, 0, dummy, 1, None) == 0
 
 
 def test_packed_bits_and_lin_dense():

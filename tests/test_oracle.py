@@ -70,3 +70,32 @@ def test_oracle_degenerate_groups():
         wq, s, b = O.quantize(w, 64, bits)
         d = O.dequantize(wq, s, b, 64, bits)
         np.testing.assert_allclose(d, w, atol=np.abs(s).max() * 1.001 + 1e-6)
+
+
+def test_oracle_epilogue_helpers_follow_the_reference_rounding():
+    """gated / lokr_residual / layernorm_modulate restate the reference's op sequences
+    (each op rounded to bf16): checked here against a step-by-step float32 evaluation."""
+    rng = np.random.default_rng(11)
+    bf = lambda a: O.to_bf16(np.asarray(a, np.float32))
+    f = O.bf16_to_f32
+    M, N, K = 6, 40, 64
+    res, gate, y = bf(rng.standard_normal((M, N))), bf(rng.standard_normal((2, N))), bf(rng.standard_normal((M, N)))
+    out = O.gated(res, gate, y, period=3)
+    rows = np.arange(M) // 3
+    want = bf(f(res) + f(bf(f(gate)[rows] * f(y))))
+    assert np.array_equal(out, want)
+    assert np.array_equal(O.gated(res, None, y), bf(f(res) + f(y)))
+    x, d = bf(rng.standard_normal((M, K))), bf(rng.standard_normal((N, K)) * 0.1)
+    r = O.lokr_residual(x, d, 0.3)
+    want = bf(f(bf(f(x).astype(np.float64) @ f(d).astype(np.float64).T)) * f(bf([0.3]))[0])
+    assert np.array_equal(r, want)
+    xs = bf(rng.standard_normal((M, 64)) * 3 + 1)
+    sc, sh = bf(rng.standard_normal(64) * 0.2), bf(rng.standard_normal(64) * 0.2)
+    n = O.layernorm_modulate(xs)
+    xf = f(xs).astype(np.float64)
+    z = (xf - xf.mean(1, keepdims=True)) / np.sqrt(xf.var(1, keepdims=True) + 1e-6)
+    assert np.array_equal(n, bf(z))
+    m = O.layernorm_modulate(xs, sc, sh)
+    assert np.array_equal(m, bf(f(bf(f(n) * f(bf(f(sc) + 1.0)))) + f(sh)))
+    m32 = O.layernorm_modulate(xs, sc, sh, f32_out=True)
+    assert np.allclose(m32, f(n) * (f(sc) + 1.0) + f(sh), rtol=0, atol=1e-6)
