@@ -743,7 +743,10 @@ bool qgemv_tc_supported(int64_t M, int64_t K, int gs, int bits, const void *x, b
     if (gs != 64 && gs != 128 && !(gs == 32 && bits == 8)) return false;  // Q4 / 32: too many accumulator columns
     if (reinterpret_cast<uintptr_t>(x) % 16) return false;
     const int64_t per_stage = 256 * 8 / bits;
-    return K % per_stage == 0 && (K / gs) % 8 == 0 && K <= (1 << 20);
+    if (K % per_stage != 0 || (K / gs) % 8 != 0 || K > (1 << 20)) return false;
+    // the activations of a CTA's K range live in shared memory: some split must fit
+    int split = 0, sps = 0;
+    return gemv3::plan(bits, gs, K, 1, 148, &split, &sps);
 }
 
 int launch_qgemv_tc(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales, const void *biases,

@@ -230,6 +230,21 @@ def test_gemv_tc_rejects_what_it_cannot_run(dev):
             qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, kernel=GEMV_TC)
 
 
+@pytest.mark.parametrize("bits,K", [(8, 32768), (4, 65536)])
+def test_gemv_long_k_falls_back(dev, bits, K):
+    """A K whose activations fit in no cluster split's shared memory: the tcgen05 GEMV
+    refuses it when forced, and the automatic choice (M = 8 would pick it) runs an
+    mma.sync GEMV instead of failing."""
+    M, N, gs = 8, 256, 64
+    _, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 3 + bits)
+    with pytest.raises(qlinear.QlError):
+        qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, kernel=GEMV_TC)
+    y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits)
+    torch.cuda.synchronize()
+    assert qlinear.device_error() == 0
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(O.quantized_matmul(x, wq, s, b, gs, bits)), what="gemv-long-k")
+
+
 @pytest.mark.parametrize("bits,gs", [(4, 64), (4, 128), (8, 32), (8, 64), (8, 128)])
 @pytest.mark.parametrize("M", [1, 3, 8])
 @pytest.mark.parametrize("K", [1024, 2048])
