@@ -223,10 +223,14 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
         if (int rc = launch_lora_t(x, M, K, e.lora_a, e.lora_rank, e.lora_scale, e.workspace, st)) return rc;
         lora_t = e.workspace;
     }
-    if (kernel == QL_KERNEL_GEMV || kernel == QL_KERNEL_GEMV_TMA || kernel == QL_KERNEL_GEMV_REGS)
-        return launch_qgemv(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size,
-                            bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y, gd,
-                            kernel == QL_KERNEL_GEMV_TMA ? 1 : kernel == QL_KERNEL_GEMV_REGS ? 2 : 0, st);
+    if (kernel == QL_KERNEL_GEMV || kernel == QL_KERNEL_GEMV_TMA || kernel == QL_KERNEL_GEMV_REGS) {
+        const int rc = launch_qgemv(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size,
+                                    bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y, gd,
+                                    kernel == QL_KERNEL_GEMV_TMA ? 1 : kernel == QL_KERNEL_GEMV_REGS ? 2 : 0, st);
+        // The GEMVs stage all of x in shared memory and refuse (before launching anything)
+        // an M * K that does not fit; the automatic choice then streams x through the GEMM.
+        if (rc != QL_EUNSUPPORTED || e.kernel != QL_KERNEL_AUTO) return rc;
+    }
     return launch_qgemm_sm100(x, M, K, wq, scales, biases, e.wq_up, e.scales_up, e.biases_up, N, group_size,
                               bits, e.bias, e.bias_up, e.act, lora_t, e.lora_b, lora ? e.lora_rank : 0, y,
                               kernel == QL_KERNEL_GEMM_PAIR ? 2 : 1, e.max_ctas, gd, e.lokr_delta, e.lokr_scale, st);

@@ -232,9 +232,9 @@ def test_gemv_tc_rejects_what_it_cannot_run(dev):
 
 @pytest.mark.parametrize("bits,K", [(8, 32768), (4, 65536)])
 def test_gemv_long_k_falls_back(dev, bits, K):
-    """A K whose activations fit in no cluster split's shared memory: the tcgen05 GEMV
-    refuses it when forced, and the automatic choice (M = 8 would pick it) runs an
-    mma.sync GEMV instead of failing."""
+    """An M * K whose activations fit no GEMV's shared memory: the tcgen05 GEMV refuses it
+    when forced, and the automatic choice (M = 8 would pick a GEMV) streams x through the
+    GEMM instead of failing (the reference takes any K)."""
     M, N, gs = 8, 256, 64
     _, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 3 + bits)
     with pytest.raises(qlinear.QlError):
