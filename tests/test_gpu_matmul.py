@@ -54,7 +54,7 @@ def test_gemv_parity(dev, bits, gs, M, K, kernel):
 @pytest.mark.parametrize("kernel", [GEMM, GEMM2])
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("gs", [32, 64, 128])
-@pytest.mark.parametrize("M,N,K", [(9, 128, 64), (256, 128, 256), (300, 200, 448), (513, 384, 128)])
+@pytest.mark.parametrize("M,N,K", [(9, 128, 64), (256, 128, 256), (300, 200, 448), (513, 384, 128), (40, 136, 96)])
 def test_gemm_parity(dev, bits, gs, M, N, K, kernel):
     if K % gs:
         pytest.skip("K must be a multiple of the group size")
