@@ -217,3 +217,37 @@ def layernorm_modulate(x, scale=None, shift=None, eps=1e-6, period=0, f32_out=Fa
         r = (r + h).astype(np.float32)
     return r.astype(np.float32) if f32_out else to_bf16(r)
 
+
+
+def _round_to(a64, bf16: bool):
+    """Round float64 values to the factors' dtype (bf16 or f32), returned as f32."""
+    a32 = np.asarray(a64, dtype=np.float64).astype(np.float32)
+    return bf16_to_f32(to_bf16(a32)) if bf16 else a32
+
+
+def _factor(f, bf16: bool):
+    """A full factor, or an (a, b) low-rank pair multiplied in the factors' dtype."""
+    if isinstance(f, tuple):
+        a, b = f
+        return _round_to(np.asarray(a, np.float64) @ np.asarray(b, np.float64), bf16)
+    return np.asarray(f, np.float32)
+
+
+def lokr_delta(scale, base_shape, f1, f2, factors_bf16=True):
+    """``scale * kron(f1, f2)`` with the reference's rounding points
+    (src/adapters.rs:71-101): low-rank products and the Kronecker product in the factors'
+    dtype, the scale applied in f32 (a one-element f32 array), one cast to bf16.  Factor
+    values are f32 arrays (bf16-representable when factors_bf16); returns bf16 bits."""
+    a = _factor(f1, factors_bf16)
+    b = _factor(f2, factors_bf16)
+    k = _round_to(np.kron(a.astype(np.float64), b.astype(np.float64)), factors_bf16)
+    return to_bf16((k * np.float32(scale)).astype(np.float32).reshape(base_shape))
+
+
+def loha_delta(scale, base_shape, w1, w2, factors_bf16=True):
+    """``scale * ((w1_a @ w1_b) * (w2_a @ w2_b))`` (src/adapters.rs:138-158); w1, w2 are
+    (a, b) pairs; rounding as lokr_delta.  Returns bf16 bits."""
+    m1 = _factor(w1, factors_bf16)
+    m2 = _factor(w2, factors_bf16)
+    h = _round_to(m1.astype(np.float64) * m2.astype(np.float64), factors_bf16)
+    return to_bf16((h * np.float32(scale)).astype(np.float32).reshape(base_shape))

@@ -1,0 +1,95 @@
+"""Load-time adapter delta reconstruction (qlinear.adapters), the input of the fused LoKr
+epilogue: LoKr ``scale * kron(w1, w2)`` and LoHa ``scale * (w1_a w1_b) * (w2_a w2_b)``
+(src/adapters.rs:25-158), against the oracle's restatement and the reference's own 2x2
+known-answer case (src/adapters.rs:695-714).  CPU only."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from qlinear import adapters as A
+from helpers import np2t, rand_bf16, t2np
+
+
+def _bits(t):
+    return t2np(t.to(torch.bfloat16))
+
+
+def test_lokr_known_answer_2x2():
+    """reconstruct_lokr_delta(alpha 8, rank 4, [2,2], w1 [[.5],[.6]], w2 [[.7,.8]]) in bf16:
+    2 * kron(w1, w2) with the f32 products rounded once."""
+    w1 = torch.tensor([[0.5], [0.6]], dtype=torch.float32)
+    w2 = torch.tensor([[0.7, 0.8]], dtype=torch.float32)
+    d = A.reconstruct_lokr_delta(8.0, 4.0, [2, 2], w1=w1, w2=w2)
+    assert d.dtype == torch.bfloat16 and tuple(d.shape) == (2, 2)
+    want = O.to_bf16((np.kron(np.float32([[0.5], [0.6]]), np.float32([[0.7, 0.8]])) * np.float32(2.0))
+                     .astype(np.float32))
+    np.testing.assert_array_equal(_bits(d), want)
+
+
+@pytest.mark.parametrize("form", ["full", "w1_lowrank", "both_lowrank"])
+def test_lokr_matches_oracle(form):
+    """bf16 factors in the three linear forms the loaders emit; a [N, K] = [96, 160]
+    delta from [8, 10] x [12, 16] factors (rank 4 products)."""
+    rng = np.random.default_rng(3)
+    a1, b1 = rand_bf16((8, 4), 0.5, rng), rand_bf16((4, 10), 0.5, rng)
+    a2, b2 = rand_bf16((12, 4), 0.5, rng), rand_bf16((4, 16), 0.5, rng)
+    w1, w2 = rand_bf16((8, 10), 0.5, rng), rand_bf16((12, 16), 0.5, rng)
+    t = lambda a: np2t(a, "cpu")
+    f = O.bf16_to_f32
+    if form == "full":
+        d = A.reconstruct_lokr_delta(16.0, 4.0, [96, 160], w1=t(w1), w2=t(w2))
+        ref = O.lokr_delta(4.0, (96, 160), f(w1), f(w2))
+    elif form == "w1_lowrank":
+        d = A.reconstruct_lokr_delta(16.0, 4.0, [96, 160], w1_a=t(a1), w1_b=t(b1), w2=t(w2))
+        ref = O.lokr_delta(4.0, (96, 160), (f(a1), f(b1)), f(w2))
+    else:
+        d = A.reconstruct_lokr_delta(16.0, 4.0, [96, 160], w1_a=t(a1), w1_b=t(b1), w2_a=t(a2), w2_b=t(b2))
+        ref = O.lokr_delta(4.0, (96, 160), (f(a1), f(b1)), (f(a2), f(b2)))
+    got = _bits(d)
+    if form == "full":
+        np.testing.assert_array_equal(got, ref)
+    else:
+        # rank-4 products: the f32 accumulation order may move a rounding by one bf16 ulp
+        diff = np.abs(got.astype(np.int32) - ref.astype(np.int32))
+        assert diff.max() <= 1 and (diff > 0).mean() < 0.01
+
+
+def test_lokr_scale_is_f32_and_promotes_bf16_factors():
+    """The scale multiplies as an f32 array: a bf16 kron times 1/3 is rounded once to bf16
+    from f32, not through a bf16 scale."""
+    w1 = torch.tensor([[1.0]], dtype=torch.bfloat16)
+    w2 = torch.tensor([[3.0, 5.0]], dtype=torch.bfloat16)
+    d = A.reconstruct_lokr_delta_scaled(1.0 / 3.0, [1, 2], w1=w1, w2=w2, out_dtype=torch.float32)
+    np.testing.assert_array_equal(d.numpy(), (np.float32([3.0, 5.0]) * np.float32(1.0 / 3.0)).reshape(1, 2))
+
+
+def test_lokr_trailing_rank_and_tucker():
+    """A 2-D w1 against a 4-D conv w2 gets trailing unit dims (make_kron); the tucker
+    rebuild is einsum('ijhw,ip,jr->prhw'); a 3-D t2 is refused."""
+    g = torch.Generator().manual_seed(0)
+    w1 = torch.randn(2, 3, generator=g)
+    t2 = torch.randn(4, 5, 3, 3, generator=g)
+    wa, wb = torch.randn(4, 6, generator=g), torch.randn(5, 7, generator=g)
+    d = A.reconstruct_lokr_delta_scaled(0.5, [12, 21, 3, 3], w1=w1, w2_t2=t2, w2_a=wa, w2_b=wb,
+                                        out_dtype=torch.float32)
+    f2 = torch.einsum("ijhw,ip,jr->prhw", t2, wa, wb)
+    np.testing.assert_allclose(d.numpy(), (torch.kron(w1[:, :, None, None].contiguous(), f2.contiguous()) * 0.5).numpy(), rtol=1e-6)
+    with pytest.raises(ValueError, match="4-D"):
+        A.reconstruct_lokr_delta_scaled(1.0, [1], w1=w1, w2_t2=t2[0], w2_a=wa, w2_b=wb)
+    with pytest.raises(ValueError, match="w1 missing"):
+        A.reconstruct_lokr_delta_scaled(1.0, [1], w2=w1)
+    with pytest.raises(ValueError, match="w2 missing"):
+        A.reconstruct_lokr_delta_scaled(1.0, [1], w1=w1, w2_a=wa)
+
+
+def test_loha_matches_oracle():
+    rng = np.random.default_rng(5)
+    a1, b1 = rand_bf16((64, 8), 0.3, rng), rand_bf16((8, 96), 0.3, rng)
+    a2, b2 = rand_bf16((64, 8), 0.3, rng), rand_bf16((8, 96), 0.3, rng)
+    t = lambda a: np2t(a, "cpu")
+    f = O.bf16_to_f32
+    d = A.reconstruct_loha_delta(0.25, [64, 96], t(a1), t(b1), t(a2), t(b2))
+    ref = O.loha_delta(0.25, (64, 96), (f(a1), f(b1)), (f(a2), f(b2)))
+    diff = np.abs(_bits(d).astype(np.int32) - ref.astype(np.int32))
+    assert diff.max() <= 1 and (diff > 0).mean() < 0.01
