@@ -78,6 +78,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                      const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_w2,
                      const __grid_constant__ CUtensorMap tm_s2, const __grid_constant__ CUtensorMap tm_b2,
                      const Params p) {
+    TL_T(tl_entry);
     using C = Cfg<BITS, SWIGLU>;
     constexpr int NPASS = C::NPASS, STAGES = C::STAGES;
     constexpr int GPS = KS / GS;                            // groups per stage
@@ -141,6 +142,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
 
     // -------------------------------------------------------------------- consumers
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    TL_T(tl_wait);
     const int tid = threadIdx.x;  // consumer thread, 0 .. CWARPS * 32 - 1
     // x -> smem, permuted so that lane c of a warp reads its four bf16 pairs of a run in
     // one 16-byte load: Q4 pairs (0,4) (1,5) (2,6) (3,7), Q8 pairs (0,2) (1,3) (4,6) (5,7)
@@ -366,6 +368,10 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             }
         }
     }
+#ifdef QL_TRACE_TL
+    named_bar_sync(1, CWARPS * 32);
+    if (threadIdx.x == 0) TL_RECORD(SWIGLU ? 5 : 4, tl_entry, tl_wait);
+#endif
 }
 
 static int make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, int rank, const uint64_t *dims,
