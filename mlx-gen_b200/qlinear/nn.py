@@ -83,7 +83,11 @@ class Lora:
     scale: float
 
     def residual(self, x: torch.Tensor) -> torch.Tensor:
-        return ((x @ self.a) @ self.b) * self.scale
+        # factors keep their loaded dtype: bf16 x with f32 factors runs (and returns) f32
+        # (src/adapters.rs:240-258); the scale is a scalar of the residual's dtype
+        dt = torch.promote_types(torch.promote_types(x.dtype, self.a.dtype), self.b.dtype)
+        r = (x.to(dt) @ self.a.to(dt)) @ self.b.to(dt)
+        return r * torch.tensor(self.scale, dtype=r.dtype, device=r.device)
 
 
 @dataclass
@@ -95,7 +99,8 @@ class Lokr:
     scale: float
 
     def residual(self, x: torch.Tensor) -> torch.Tensor:
-        return (x @ self.delta.to(x.dtype).t()) * self.scale
+        r = x @ self.delta.to(x.dtype).t()
+        return r * torch.tensor(self.scale, dtype=r.dtype, device=r.device)
 
 
 Adapter = Union[Lora, Lokr]
@@ -168,14 +173,17 @@ class AdaptableLinear:
     # ---- forward (src/adapters.rs:543-549)
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """``base(x) + sum residual(x)``.  A quantized base with bf16 activations and at
-        most one LoRA plus at most one LoKr adapter runs as ONE fused kernel (the LoRA
-        residual accumulates into the same fp32 tile, the LoKr delta is added to the
-        dequantized weights); any other stack adds the residuals separately."""
+        most one LoRA (bf16 factors) plus at most one LoKr adapter runs as ONE fused kernel
+        (the LoRA residual accumulates into the same fp32 tile, the LoKr delta is added to
+        the dequantized weights); any other stack adds the residuals separately, with the
+        reference's dtype promotion (f32 factors make the output f32)."""
         loras = [a for a in self.adapters if isinstance(a, Lora)]
         lokrs = [a for a in self.adapters if isinstance(a, Lokr)]
+        # f32 LoRA factors promote the reference's output to f32: that stack is not fused
         if (isinstance(self.base, QuantizedLinear) and x.dtype == torch.bfloat16
                 and self.base.scales.dtype == torch.bfloat16 and self.adapters
-                and len(loras) <= 1 and len(lokrs) <= 1):
+                and len(loras) <= 1 and len(lokrs) <= 1
+                and all(l.a.dtype == torch.bfloat16 and l.b.dtype == torch.bfloat16 for l in loras)):
             lo = (loras[0].a, loras[0].b, loras[0].scale) if loras else None
             lk = (lokrs[0].delta, lokrs[0].scale) if lokrs else None
             return self.base.forward(x, lora=lo, lokr=lk)

@@ -93,3 +93,30 @@ def test_loha_matches_oracle():
     ref = O.loha_delta(0.25, (64, 96), (f(a1), f(b1)), (f(a2), f(b2)))
     diff = np.abs(_bits(d).astype(np.int32) - ref.astype(np.int32))
     assert diff.max() <= 1 and (diff > 0).mean() < 0.01
+
+
+def test_adapter_residual_dtypes_follow_the_reference():
+    """Adapter::residual (src/adapters.rs:240-270): LoRA factors keep their dtype, so bf16 x
+    with f32 factors gives an f32 residual and an f32 output; bf16 factors stay bf16 with
+    the scale rounded to bf16; a LoKr delta is cast to x's dtype."""
+    from qlinear import AdaptableLinear, Lokr, Lora
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(3, 16, generator=g).to(torch.bfloat16)
+    a32, b32 = torch.randn(16, 4, generator=g), torch.randn(4, 8, generator=g) * 0.1
+    r = Lora(a32, b32, 0.5).residual(x)
+    assert r.dtype == torch.float32
+    torch.testing.assert_close(r, ((x.float() @ a32) @ b32) * 0.5, rtol=0, atol=0)
+    a16, b16 = a32.to(torch.bfloat16), b32.to(torch.bfloat16)
+    r16 = Lora(a16, b16, 0.3).residual(x)
+    assert r16.dtype == torch.bfloat16
+    assert torch.equal(r16, ((x @ a16) @ b16) * torch.tensor(0.3, dtype=torch.bfloat16))
+    w = (torch.randn(8, 16, generator=g) * 0.1).to(torch.bfloat16)
+    lin = AdaptableLinear.dense(w)
+    lin.push(Lora(a32, b32, 0.5))
+    y = lin(x)
+    assert y.dtype == torch.float32
+    torch.testing.assert_close(y, (x @ w.t()).float() + r, rtol=0, atol=0)
+    delta = torch.randn(8, 16, generator=g)
+    rk = Lokr(delta, 2.0).residual(x)
+    assert rk.dtype == torch.bfloat16
+    assert torch.equal(rk, (x @ delta.to(torch.bfloat16).t()) * 2.0)

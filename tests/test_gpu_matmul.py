@@ -324,3 +324,23 @@ def test_lokr_with_lora_and_gate_through_adaptable_linear(dev):
     base = O.quantized_matmul(x, wq, s, b, gs, bits, lora_a=A, lora_b=B, lora_scale=0.5)
     ref = O.add_bf16(base, O.lokr_residual(x, delta, 2.0))
     assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), ulps=4, atol_frac=2 ** -7, what="lora+lokr")
+
+
+def test_adaptable_linear_f32_lora_factors_promote_to_f32(dev):
+    """f32 LoRA factors (the reference goldens' dtype) on a quantized base with bf16 x:
+    the reference's output is the bf16 base plus an f32 residual, promoted to f32
+    (src/adapters.rs:240-258), so the stack runs unfused: the base on libqlinear, the
+    residual in f32."""
+    M, N, K, gs, bits = 40, 256, 512, 64, 4
+    rng, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 91)
+    A = (rng.standard_normal((K, 8)) / np.sqrt(8)).astype(np.float32)
+    B = (rng.standard_normal((8, N)) * 0.01).astype(np.float32)
+    lin = qlinear.AdaptableLinear.from_quantized_parts(wqt, st, bt, None, gs, bits)
+    lin.push(qlinear.Lora(torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev), 0.5))
+    y = lin.forward(xt)
+    torch.cuda.synchronize()
+    assert y.dtype == torch.float32 and qlinear.device_error() == 0
+    base = O.to_f32(O.quantized_matmul(x, wq, s, b, gs, bits)).astype(np.float64)
+    res = (O.to_f32(x).astype(np.float64) @ A @ B) * 0.5
+    got = y.cpu().numpy().astype(np.float64)
+    assert np.abs(got - (base + res)).max() <= 2 ** -7 * np.abs(base).max() + 1e-4
