@@ -132,8 +132,8 @@ def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, bi
     ``silu(x W^T) * (x W3^T)``).  lora: ``(A [K, r], B [r, N], scale)`` adds
     ``scale * (x.A).B``.  lokr: ``(delta [N, K], scale)`` adds ``scale * x.delta^T``
     (src/adapters.rs:263-266), fused into the dequantized weights.  residual / gate: the gated residual ``residual + gate * y``
-    (src/nn.rs:166-176), gate ``[N]`` or ``[M / gate_period, N]``.  Output dtype = x's
-    dtype."""
+    (src/nn.rs:166-176), gate ``[N]`` or ``[M / gate_period, N]``.  Output dtype =
+    promote(x, scales), as mlx's; bias, residual and gate are taken in that dtype."""
     _need_cuda(x, wq, scales, biases, bias)
     if not transpose:
         raise NotImplementedError("only transpose=True is supported (the reference's only form)")
@@ -142,11 +142,13 @@ def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, bi
     lead = x.shape[:-1]
     x2 = x.reshape(-1, K).contiguous()
     M = x2.shape[0]
-    y = out if out is not None else torch.empty((*lead, N), dtype=x.dtype, device=x.device)
+    # mlx's quantized_matmul returns promote(x, scales): bf16 x with f32 scales gives f32
+    ydt = torch.promote_types(x.dtype, scales.dtype)
+    y = out if out is not None else torch.empty((*lead, N), dtype=ydt, device=x.device)
     ep = Epilogue()
     keep = []  # tensors whose memory the call reads
     if bias is not None:
-        bias = bias.to(x.dtype).contiguous()
+        bias = bias.to(y.dtype).contiguous()
         keep.append(bias)
         ep.bias = bias.data_ptr()
     ep.act = _ACTS[act]
@@ -157,7 +159,7 @@ def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, bi
         keep += [uq, us, ub]
         ep.wq_up, ep.scales_up, ep.biases_up = uq.data_ptr(), us.data_ptr(), ub.data_ptr()
         if len(up) > 3 and up[3] is not None:
-            ubias = up[3].to(x.dtype).contiguous()
+            ubias = up[3].to(y.dtype).contiguous()
             keep.append(ubias)
             ep.bias_up = ubias.data_ptr()
     if lora is not None:

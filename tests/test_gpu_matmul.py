@@ -344,3 +344,17 @@ def test_adaptable_linear_f32_lora_factors_promote_to_f32(dev):
     res = (O.to_f32(x).astype(np.float64) @ A @ B) * 0.5
     got = y.cpu().numpy().astype(np.float64)
     assert np.abs(got - (base + res)).max() <= 2 ** -7 * np.abs(base).max() + 1e-4
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_output_dtype_promotes_like_mlx(golden, dev, bits):
+    """bf16 activations against the fixture's f32 scales: mlx's quantized_matmul returns
+    promote(bf16, f32) = f32 (the generic kernel serves the mixed case)."""
+    p = f"q{bits}_"
+    xb = O.to_bf16(golden["x"].astype(np.float32))
+    y = qlinear.quantized_matmul(np2t(xb, dev), np2t(golden[p + "wq"], dev), np2t(golden[p + "scales"], dev),
+                                 np2t(golden[p + "biases"], dev), True, 64, bits)
+    assert y.dtype == torch.float32
+    w = O.dequantize(golden[p + "wq"], golden[p + "scales"], golden[p + "biases"], 64, bits).astype(np.float64)
+    ref = O.to_f32(xb).astype(np.float64) @ w.T
+    np.testing.assert_allclose(t2np(y), ref, rtol=1e-4, atol=1e-3)
