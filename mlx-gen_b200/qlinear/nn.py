@@ -32,11 +32,15 @@ class Linear:
     bias: Optional[torch.Tensor] = None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        # fused addmm: one rounding of x.W^T + b (src/adapters.rs:286-298)
-        w = self.weight.to(x.dtype) if self.weight.dtype != x.dtype else self.weight
+        # fused addmm: one rounding of x.W^T + b (src/adapters.rs:286-298), in the promoted
+        # dtype of x, W and b (bf16 x against f32 weights computes in f32, as mlx does)
+        dt = torch.promote_types(x.dtype, self.weight.dtype)
+        if self.bias is not None:
+            dt = torch.promote_types(dt, self.bias.dtype)
+        w, x = self.weight.to(dt), x.to(dt)
         if self.bias is None:
             return x @ w.t()
-        return torch.addmm(self.bias.to(x.dtype), x.reshape(-1, x.shape[-1]), w.t()).reshape(
+        return torch.addmm(self.bias.to(dt), x.reshape(-1, x.shape[-1]), w.t()).reshape(
             *x.shape[:-1], w.shape[0])
 
 

@@ -120,3 +120,55 @@ def test_adapter_residual_dtypes_follow_the_reference():
     rk = Lokr(delta, 2.0).residual(x)
     assert rk.dtype == torch.bfloat16
     assert torch.equal(rk, (x @ delta.to(torch.bfloat16).t()) * 2.0)
+
+
+def _dense_case():
+    """The reference's deterministic 64x64 case (src/adapters.rs:840-870)."""
+    i = torch.arange(64 * 64, dtype=torch.float32)
+    w = (torch.sin(i * 0.013) * 0.05).reshape(64, 64).to(torch.bfloat16)
+    bias = (torch.cos(torch.arange(64, dtype=torch.float32) * 0.7) * 0.1).to(torch.bfloat16)
+    x = (torch.sin(torch.arange(4 * 64, dtype=torch.float32) * 0.031) * 0.5).reshape(4, 64)
+    return w, bias, x
+
+
+def test_biased_dense_forward_is_fused_addmm():
+    """bf16 activations: bit-exact to addmm(bias, x, W^T) and not the double-rounded
+    matmul + add; f32 activations: addmm == matmul + add bit for bit."""
+    from qlinear import AdaptableLinear
+    w, bias, x = _dense_case()
+    xb = x.to(torch.bfloat16)
+    got = AdaptableLinear.dense(w, bias)(xb)
+    assert torch.equal(got, torch.addmm(bias, xb, w.t()))
+    assert not torch.equal(got, xb @ w.t() + bias)
+    got32 = AdaptableLinear.dense(w, bias)(x)
+    assert got32.dtype == torch.float32
+    assert torch.equal(got32, x @ w.float().t() + bias.float())
+
+
+def test_scale_zero_lokr_is_a_bit_exact_noop_and_stacks_sum():
+    from qlinear import AdaptableLinear, Lokr, Lora
+    w = torch.tensor([[0.1, 0.2], [0.3, 0.4]])
+    x = torch.tensor([[1.0, 2.0]])
+    lin = AdaptableLinear.dense(w)
+    base = lin(x)
+    delta = A.reconstruct_lokr_delta(8.0, 4.0, [2, 2], w1=torch.tensor([[0.5], [0.6]]),
+                                     w2=torch.tensor([[0.7, 0.8]]))
+    lin.push(Lokr(delta, 0.0))
+    assert torch.equal(lin(x), base)
+    # mixed LoRA + LoKr: the residuals are summed over one base application
+    a, b = torch.tensor([[0.5], [-0.25]]), torch.tensor([[1.0, 2.0]])
+    lin.set_adapters([Lora(a, b, 0.5), Lokr(delta, 1.0)])
+    want = base + ((x @ a) @ b) * 0.5 + x @ delta.float().t()
+    assert torch.equal(lin(x), want)
+
+
+def test_merge_into_a_quantized_base_is_refused():
+    """src/adapters.rs:414-426: a LoRA must be merged before quantization."""
+    from qlinear import AdaptableLinear
+    q = AdaptableLinear.from_quantized_parts(torch.zeros(4, 8, dtype=torch.int32), torch.ones(4, 1),
+                                             torch.zeros(4, 1), None, 64, 4)
+    with pytest.raises(ValueError, match="quantized"):
+        q.merge_dense_delta(torch.zeros(4, 64))
+    d = AdaptableLinear.dense(torch.zeros(2, 2))
+    d.merge_dense_delta(torch.ones(2, 2))
+    assert torch.equal(d.dense_weight()[0], torch.ones(2, 2))

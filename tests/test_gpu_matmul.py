@@ -358,3 +358,54 @@ def test_output_dtype_promotes_like_mlx(golden, dev, bits):
     w = O.dequantize(golden[p + "wq"], golden[p + "scales"], golden[p + "biases"], 64, bits).astype(np.float64)
     ref = O.to_f32(xb).astype(np.float64) @ w.T
     np.testing.assert_allclose(t2np(y), ref, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_adaptable_linear_quantize_matches_bf16_reference(golden, dev, bits):
+    """AdaptableLinear.quantize quantizes the bf16-cast weight (tests/quant_parity.rs:68-96):
+    its forward on the fixture's f32 x matches the oracle's quantize(bf16(w)) + qmm within
+    the reference's (1e-3, 1e-4)."""
+    lin = qlinear.AdaptableLinear.dense(torch.from_numpy(golden["w"]).to(dev))
+    assert not lin.is_quantized()
+    lin.quantize(bits)
+    assert lin.is_quantized()
+    out = lin(torch.from_numpy(golden["x"]).to(dev))
+    assert out.dtype == torch.float32
+    wq, s, b = O.quantize(O.to_bf16(golden["w"]), 64, bits)
+    ref = O.to_f32(O.quantized_matmul(golden["x"], wq, s, b, 64, bits))
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-3, atol=1e-4)
+
+
+def test_quantized_forward_approximates_dense(golden, dev):
+    """Peak-relative error against the dense forward: Q8 < 2 %, Q4 < 12 %
+    (tests/quant_parity.rs:98-127)."""
+    w = torch.from_numpy(golden["w"]).to(dev)
+    x = torch.from_numpy(golden["x"]).to(dev)
+    dense = qlinear.AdaptableLinear.dense(w)(x)
+    peak = dense.abs().max().item()
+    for bits, max_rel in [(8, 0.02), (4, 0.12)]:
+        q = qlinear.AdaptableLinear.dense(w)
+        q.quantize(bits)
+        assert (q(x) - dense).abs().max().item() / peak < max_rel
+
+
+def test_q8_forward_close_to_dense_across_shapes(dev):
+    """Q8 forward vs the f32 dense forward over the transformer's linear shapes at M = 4,
+    f32 and bf16 activations, bias 0.1: mean relative error < 5 %
+    (mlx-gen-qwen-image/tests/q8_smoke.rs:15-60)."""
+    g = torch.Generator(device=dev).manual_seed(0)
+    worst = 0.0
+    for out, inn in [(3072, 64), (3072, 128), (3072, 3072), (3072, 3584), (64, 3072)]:
+        w = torch.randn(out, inn, device=dev, generator=g).to(torch.bfloat16)
+        b = torch.full((out,), 0.1, device=dev).to(torch.bfloat16)
+        x32 = torch.randn(1, 4, inn, device=dev, generator=g)
+        lin = qlinear.AdaptableLinear.dense(w, b)
+        d32 = lin(x32)
+        lin.quantize(8)
+        q32, q16 = lin(x32), lin(x32.to(torch.bfloat16))
+        assert q32.shape == q16.shape == (1, 4, out)
+        for q in (q32, q16):
+            worst = max(worst, ((q.float() - d32).abs().sum() / d32.abs().sum()).item())
+    torch.cuda.synchronize()
+    assert qlinear.device_error() == 0
+    assert worst < 0.05, worst
