@@ -130,8 +130,9 @@ int ql_dequantize(const uint32_t *wq, const void *scales, const void *biases, in
 
 /* Replaces the quantized TokenEmbedding gather: take_axis(wq|scales|biases, ids)
  * followed by dequantize and a cast (src/nn.rs:42-59).  ids [R] int64 into the
- * N rows; out [R, K] in out_dtype.  An id outside [0, N) yields a zero row and
- * sets the device error word. */
+ * N rows; out [R, K] in out_dtype.  Each value is fma(code, scale, bias) in fp32
+ * rounded to sb_dtype (dequantize's output dtype), then converted to out_dtype.  An id
+ * outside [0, N) yields a zero row and sets the device error word. */
 int ql_dequantize_rows(const int64_t *ids, int64_t R, const uint32_t *wq, const void *scales,
                        const void *biases, int sb_dtype, int64_t N, int64_t K, int group_size,
                        int bits, void *out, int out_dtype, void *stream);

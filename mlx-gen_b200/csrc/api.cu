@@ -32,7 +32,7 @@ int fail(int status, const char *fmt, ...) {
 int launch_quantize(const void *, int, int64_t, int64_t, int, int, uint32_t *, void *, void *, int,
                     cudaStream_t);
 int launch_dequantize(const int64_t *, int64_t, int64_t, int64_t, int, int, const uint32_t *,
-                      const void *, const void *, int, void *, int, cudaStream_t);
+                      const void *, const void *, int, void *, int, bool, cudaStream_t);
 int launch_qgemv(const void *, int64_t, int64_t, const uint32_t *, const void *, const void *,
                  const uint32_t *, const void *, const void *, int64_t, int, int, const void *,
                  const void *, int, const void *, const void *, int64_t, void *, const Gated &, int, cudaStream_t);
@@ -116,7 +116,7 @@ int ql_dequantize(const uint32_t *wq, const void *scales, const void *biases, in
     if (!aligned16(wq) || !aligned16(out))
         return fail(QL_EINVAL_ARG, "ql_dequantize: wq and out must be 16-byte aligned");
     return launch_dequantize(nullptr, N, N, K, group_size, bits, wq, scales, biases, sb_dtype, out,
-                             out_dtype, (cudaStream_t)stream);
+                             out_dtype, false, (cudaStream_t)stream);
 }
 
 int ql_layernorm_modulate(const void *x, int64_t M, int64_t D, float eps, const void *scale, const void *shift,
@@ -144,7 +144,7 @@ int ql_dequantize_rows(const int64_t *ids, int64_t R, const uint32_t *wq, const 
     if (!aligned16(wq) || !aligned16(out))
         return fail(QL_EINVAL_ARG, "ql_dequantize_rows: wq and out must be 16-byte aligned");
     return launch_dequantize(ids, R, N, K, group_size, bits, wq, scales, biases, sb_dtype, out,
-                             out_dtype, (cudaStream_t)stream);
+                             out_dtype, true, (cudaStream_t)stream);
 }
 
 size_t ql_matmul_workspace_size(int64_t M, int64_t N, int64_t K, const ql_epilogue *ep) {

@@ -70,6 +70,13 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return r;
 }
 
+// v rounded to the precision of dtype dt (QL_F32 / QL_BF16 / QL_F16), returned as f32
+__device__ __forceinline__ float round_to(int dt, float v) {
+    if (dt == QL_F32) return v;
+    if (dt == QL_BF16) return round_bf16(v);
+    return __half2float(__float2half_rn(v));
+}
+
 __device__ __forceinline__ float bf16lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 

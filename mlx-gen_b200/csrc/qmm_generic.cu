@@ -15,11 +15,6 @@ namespace generic {
 
 constexpr int TM = 32, TN = 32, TK = 32;  // 256 threads, 2x2 outputs each
 
-__device__ __forceinline__ float round_to(int dt, float v) {
-    if (dt == QL_F32) return v;
-    if (dt == QL_BF16) return round_bf16(v);
-    return __half2float(__float2half_rn(v));
-}
 
 struct Params {
     const void *x;

@@ -114,12 +114,14 @@ __global__ void __launch_bounds__(256) quantize_kernel(const void *__restrict__ 
 }
 
 // One thread per packed word of the output rows.  ids == nullptr: row r reads
-// packed row r; otherwise packed row ids[r] (quantized embedding gather).
+// packed row r; otherwise packed row ids[r] (quantized embedding gather).  round_sb: the
+// value is first rounded to the scales' dtype (mlx's dequantize output) and then converted
+// to out_dtype, as the reference's gather + dequantize + cast does.
 template <int BITS>
 __global__ void __launch_bounds__(256) dequantize_kernel(
     const int64_t *__restrict__ ids, int64_t rows, int64_t N, int64_t words_per_row, int gs,
     const uint32_t *__restrict__ wq, const void *__restrict__ scales,
-    const void *__restrict__ biases, int sb_dtype, void *__restrict__ out, int out_dtype) {
+    const void *__restrict__ biases, int sb_dtype, void *__restrict__ out, int out_dtype, bool round_sb) {
     constexpr int EPW = 32 / BITS;
     const int64_t total = rows * words_per_row;
     const int64_t G = words_per_row * EPW / gs;
@@ -142,8 +144,10 @@ __global__ void __launch_bounds__(256) dequantize_kernel(
             const float s = load_as_f32(scales, sb_dtype, g);
             const float b = load_as_f32(biases, sb_dtype, g);
 #pragma unroll
-            for (int i = 0; i < EPW; ++i)
+            for (int i = 0; i < EPW; ++i) {
                 o[i] = fmaf((float)((word >> (BITS * i)) & ((1u << BITS) - 1u)), s, b);
+                if (round_sb) o[i] = round_to(sb_dtype, o[i]);
+            }
         } else {
 #pragma unroll
             for (int i = 0; i < EPW; ++i) o[i] = 0.f;
@@ -198,15 +202,15 @@ int launch_quantize(const void *w, int w_dtype, int64_t N, int64_t K, int gs, in
 
 int launch_dequantize(const int64_t *ids, int64_t rows, int64_t N, int64_t K, int gs, int bits,
                       const uint32_t *wq, const void *scales, const void *biases, int sb_dtype,
-                      void *out, int out_dtype, cudaStream_t st) {
+                      void *out, int out_dtype, bool round_sb, cudaStream_t st) {
     const int64_t wpr = K * bits / 32;
     const int grid = grid_for(rows * wpr, 256);
     if (bits == 4)
         dequantize_kernel<4><<<grid, 256, 0, st>>>(ids, rows, N, wpr, gs, wq, scales, biases,
-                                                    sb_dtype, out, out_dtype);
+                                                    sb_dtype, out, out_dtype, round_sb);
     else
         dequantize_kernel<8><<<grid, 256, 0, st>>>(ids, rows, N, wpr, gs, wq, scales, biases,
-                                                    sb_dtype, out, out_dtype);
+                                                    sb_dtype, out, out_dtype, round_sb);
     QL_CUDA_TRY(cudaGetLastError());
     return QL_OK;
 }

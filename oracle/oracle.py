@@ -99,6 +99,14 @@ def quantize(w: np.ndarray, group_size: int = 64, bits: int = 4, sb_dtype: int |
 
 
 def dequantize(wq, scales, biases, group_size=64, bits=4, ids=None, out_dtype=None):
+    """mlx affine dequantize (src/nn.rs:55): fma(code, scale, bias) rounded once to
+    out_dtype (default: the scales' dtype).  With ids: the quantized embedding gather
+    (src/nn.rs:42-59), rows ids of the dequantized table in the scales' dtype, then cast
+    to out_dtype."""
+    if ids is not None and out_dtype is not None and out_dtype != dtype_code(scales):
+        rows = dequantize(wq, scales, biases, group_size, bits, ids=ids)
+        f = to_f32(rows)
+        return {F32: lambda: f, BF16: lambda: to_bf16(f), F16: lambda: f.astype(np.float16)}[out_dtype]()
     wq = np.ascontiguousarray(wq, np.uint32)
     N, G = scales.shape
     K = G * group_size

@@ -64,7 +64,9 @@ def test_quantize_edge_values(dev, bits):
 
 @pytest.mark.parametrize("bits", [4, 8])
 def test_dequantize_rows_gather(dev, bits):
-    """Quantized embedding gather (src/nn.rs:42-59): f32 rows, ids of any shape."""
+    """Quantized embedding gather (src/nn.rs:42-59): f32 rows, ids of any shape; values
+    are dequantized in the scales' dtype (bf16) and then widened, as the reference's
+    dequantize + cast, so every f32 output is bf16-representable."""
     rng = np.random.default_rng(11)
     w = rand_bf16((500, 256), 0.02, rng)
     wq, s, b = qlinear.quantize(np2t(w, dev), 64, bits)
@@ -73,6 +75,7 @@ def test_dequantize_rows_gather(dev, bits):
     ref = O.dequantize(t2np(wq), t2np(s), t2np(b), 64, bits, ids=ids, out_dtype=O.F32)
     assert got.shape == (3, 7, 256)
     assert np.array_equal(t2np(got).reshape(-1, 256), ref)
+    assert np.array_equal(O.bf16_to_f32(O.to_bf16(ref)), ref)
     emb = qlinear.TokenEmbedding(np2t(w, dev))
     emb.quantize(bits, cast_to_bf16=True)
     assert np.array_equal(t2np(emb(torch.from_numpy(ids).to(dev))).reshape(-1, 256), ref)
