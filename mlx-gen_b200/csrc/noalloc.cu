@@ -26,7 +26,6 @@
 namespace ql {
 
 constexpr size_t kNoAllocScratchBytes = 8u << 20;
-constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

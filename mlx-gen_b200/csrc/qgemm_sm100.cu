@@ -638,14 +638,14 @@ static int launch_t(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensor
                     const CUtensorMap &mt, const Params &p, const Gated &gd, int max_ctas, cudaStream_t st) {
     using C = Cfg<BITS, CG>;
     auto kfn = GATED ? (const void *)qgemm_gated_kernel<BITS, SWIGLU, CG> : (const void *)qgemm_kernel<BITS, SWIGLU, CG>;
-    static bool configured = false;  // per template instance; attribute is per-function
-    if (!configured) {
-        QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_TOTAL));
-        if (CG == 2) QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-        configured = true;
-    }
+    static PerDeviceFlag configured;  // per template instance and device
     int dev = 0, sms = 148;
     QL_CUDA_TRY(cudaGetDevice(&dev));
+    if (!configured.test(dev)) {
+        QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_TOTAL));
+        if (CG == 2) QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        configured.set(dev);
+    }
     QL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int tiles = p.num_w_tiles * p.num_t_tiles;
     cudaLaunchConfig_t cfg = {};
@@ -661,12 +661,14 @@ static int launch_t(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensor
     cfg.numAttrs = CG == 2 ? 1 : 0;  // a plain launch for the 1-CTA kernel
     // persistent grid: as many clusters as can be resident at once (pairs need two free
     // SMs of one GPC), never more than there are tiles
-    static int max_clusters = 0;
+    static PerDeviceInt resident;
+    int max_clusters = resident.get(dev);
     if (!max_clusters) {
         cfg.gridDim = dim3((unsigned)((sms / CG) * CG));
         int mc = 0;
         if (CG == 1 || cudaOccupancyMaxActiveClusters(&mc, kfn, &cfg) != cudaSuccess || mc <= 0) mc = sms / CG;
         max_clusters = mc;
+        resident.put(dev, mc);
         if (getenv("QL_DEBUG")) fprintf(stderr, "qgemm CG=%d: %d resident clusters, smem %d\n", CG, mc, C::SMEM_TOTAL);
     }
     int clusters = tiles < max_clusters ? tiles : max_clusters;
@@ -684,13 +686,13 @@ static int launch_lokr(const CUtensorMap &mx, const CUtensorMap &mw, const CUten
                        const CUtensorMap &md, const LokrArgs &la, int max_ctas, cudaStream_t st) {
     using C = Cfg<BITS, 1, true>;
     auto kfn = qgemm_lokr_kernel<BITS, GATED>;
-    static bool configured = false;
-    if (!configured) {
-        QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_TOTAL));
-        configured = true;
-    }
+    static PerDeviceFlag configured;
     int dev = 0, sms = 148;
     QL_CUDA_TRY(cudaGetDevice(&dev));
+    if (!configured.test(dev)) {
+        QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_TOTAL));
+        configured.set(dev);
+    }
     QL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int tiles = p.num_w_tiles * p.num_t_tiles;
     int ctas = tiles < sms ? tiles : sms;

@@ -314,12 +314,13 @@ int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const 
     // The tcgen05 kernel wins once its row tiles (128 rows, 64 with SwiGLU) fill the GPU,
     // or at 6+ tokens (the mma.sync kernel's per-token folds grow with M); below that its
     // fixed start-up (TMEM, activation conversion, pipeline fill) dominates.
-    static int n_sms = 0;
+    static PerDeviceInt sm_count;
+    const int cur_dev = current_device();
+    int n_sms = sm_count.get(cur_dev);
     if (!n_sms) {
-        int dev = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess ||
-            cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        if (cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, cur_dev) != cudaSuccess || n_sms <= 0)
             n_sms = 148;
+        sm_count.put(cur_dev, n_sms);
     }
     static const bool force_tc = getenv("QL_GEMV_TC") != nullptr;
     const int64_t tiles = (N + (act == QL_ACT_SWIGLU ? 63 : 127)) / (act == QL_ACT_SWIGLU ? 64 : 128);

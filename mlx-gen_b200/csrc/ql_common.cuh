@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/qlinear.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
@@ -19,6 +21,30 @@
 #endif
 
 namespace ql {
+
+// Host-side set-up done once per device (kernel attributes belong to a device's context;
+// calls may come from several threads and devices, and repeating the set-up is harmless).
+constexpr int kMaxDevices = 64;
+struct PerDeviceFlag {
+    std::atomic<uint64_t> mask{0};
+    bool test(int dev) const {  // devices past the mask are set up on every call
+        return dev < kMaxDevices && ((mask.load(std::memory_order_acquire) >> dev) & 1u);
+    }
+    void set(int dev) {
+        if (dev < kMaxDevices) mask.fetch_or(1ull << dev, std::memory_order_release);
+    }
+};
+struct PerDeviceInt {  // 0 = not yet known
+    std::atomic<int> v[kMaxDevices];
+    int get(int dev) const { return dev < kMaxDevices ? v[dev].load(std::memory_order_relaxed) : 0; }
+    void put(int dev, int x) {
+        if (dev < kMaxDevices) v[dev].store(x, std::memory_order_relaxed);
+    }
+};
+inline int current_device() {
+    int d = 0;
+    return cudaGetDevice(&d) == cudaSuccess ? d : 0;
+}
 
 // ------------------------------------------------------------------ host errors
 

@@ -320,13 +320,14 @@ int launch_lora_t(const void *x, int64_t M, int64_t K, const void *A, int64_t ra
     using namespace generic::lt;
     const int vec_a = rank % 8 == 0 && reinterpret_cast<uintptr_t>(A) % 16 == 0;
     const dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)(rpad / BN));
-    static bool configured = false;
-    if (!configured) {
+    static PerDeviceFlag configured;
+    const int cur_dev = current_device();
+    if (!configured.test(cur_dev)) {
         QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-        configured = true;
+        configured.set(cur_dev);
     }
     CUtensorMap mx{}, ma{};
     if (vec_a) {
