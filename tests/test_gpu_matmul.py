@@ -409,3 +409,23 @@ def test_q8_forward_close_to_dense_across_shapes(dev):
     torch.cuda.synchronize()
     assert qlinear.device_error() == 0
     assert worst < 0.05, worst
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_one_process_drives_two_gpus():
+    """Kernel attributes are per device: the same entry points called on cuda:0 and then
+    cuda:1 from one process (GEMM, GEMM with LoRA, GEMV) give the same results."""
+    outs = []
+    for d in (0, 1):
+        dev = torch.device(f"cuda:{d}")
+        with torch.cuda.device(dev):
+            rng, x, wq, s, b, xt, wqt, st, bt = make_case(dev, 300, 256, 512, 64, 4, 7)
+            A = rand_bf16((512, 16), 0.25, rng)
+            B = rand_bf16((16, 256), 0.01, rng)
+            y1 = qlinear.quantized_matmul(xt, wqt, st, bt, True, 64, 4)
+            y2 = qlinear.quantized_matmul(xt, wqt, st, bt, True, 64, 4, lora=(np2t(A, dev), np2t(B, dev), 0.5))
+            y3 = qlinear.quantized_matmul(xt[:2].contiguous(), wqt, st, bt, True, 64, 4)
+            torch.cuda.synchronize(dev)
+            outs.append([t2np(y) for y in (y1, y2, y3)])
+    for a, b in zip(*outs):
+        assert np.array_equal(a, b)
