@@ -603,25 +603,55 @@ def run_ours(args):
                                   "per_launch_ms": {k: statistics.mean(v) for k, v in per.items()}}
     # e2e through the public API with host buffers.  N > 1: every rank moves 1/N of the rows
     # over its own PCIe link -- its slice of x up (then an NCCL all-gather over NVLink gives
-    # every rank the whole input) and its slice of the block output down
+    # every rank the whole input) and its slice of the block output down.  Each step's
+    # copies are issued on two copy streams (double-buffered device and pinned host
+    # buffers), so step i+1's upload and step i-1's download run on the copy engines
+    # under step i's GEMMs; every copy of every step is inside the timed region.
     rows = M // world
     xh = x[rank * rows:(rank + 1) * rows].cpu().pin_memory()
     out_t, out_rows = blk.result_rows()
-    yh = torch.empty(rows, cfg["hidden"], dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty_like(x)
-    xd_part = xd[rank * rows:(rank + 1) * rows]
+    comp = blk.main
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    xd2 = [torch.empty_like(x) for _ in range(2)]
+    yd2 = [torch.empty(rows, cfg["hidden"], dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    yh2 = [torch.empty(rows, cfg["hidden"], dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    in_ready, in_free, out_ready, out_free = ([torch.cuda.Event() for _ in range(2)] for _ in range(4))
+
+    def own_rows(y):
+        return y if out_rows < M else y[rank * rows:(rank + 1) * rows]
+
+    y_expect = own_rows(step(xin=x, need_result=True)).cpu()  # checks what the pipeline delivers
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    t0.record()
-    for _ in range(args.steps):
-        xd_part.copy_(xh, non_blocking=True)
+    t0.record(comp)
+    s_in.wait_stream(comp)
+    s_out.wait_stream(comp)
+    for i in range(args.steps):
+        j = i % 2
+        xpart = xd2[j][rank * rows:(rank + 1) * rows]
+        if i >= 2:
+            s_in.wait_event(in_free[j])  # step i-2 has consumed this input buffer
+        with torch.cuda.stream(s_in):
+            xpart.copy_(xh, non_blocking=True)
+        in_ready[j].record(s_in)
+        comp.wait_event(in_ready[j])
         if world > 1:
-            dist.all_gather_into_tensor(xd, xd_part)
-        y = step(xin=xd, need_result=True)
-        yh.copy_(y if out_rows < M else y[rank * rows:(rank + 1) * rows], non_blocking=True)
-    t1.record()
+            dist.all_gather_into_tensor(xd2[j], xpart)
+        y = step(xin=xd2[j], need_result=True)
+        in_free[j].record(comp)
+        if i >= 2:
+            comp.wait_event(out_free[j])  # step i-2's download has left this buffer
+        yd2[j].copy_(own_rows(y))
+        out_ready[j].record(comp)
+        s_out.wait_event(out_ready[j])
+        with torch.cuda.stream(s_out):
+            yh2[j].copy_(yd2[j], non_blocking=True)
+        out_free[j].record(s_out)
+    comp.wait_stream(s_out)
+    t1.record(comp)
     torch.cuda.synchronize()
+    assert torch.equal(yh2[(args.steps - 1) % 2], y_expect), "pipelined e2e delivered a wrong block output"
     e2e_ms = t0.elapsed_time(t1) / args.steps
     if world > 1:
         tt = torch.tensor([e2e_ms], device=dev)
@@ -631,7 +661,7 @@ def run_ours(args):
     # at every N with the same tensor-parallel scheme
     wan = None
     if not args.no_extras:
-        del blk, x, xd
+        del blk, x, xd2, yd2
         torch.cuda.empty_cache()
         wblk = TPBlock(dict(WAN), wan_linears, dev, 4, rank, world, args.comm_sms, chunks=4, mode="seqpar")
         wms = time_block(wblk, steps=5, warmup=2, world=world)
@@ -650,7 +680,8 @@ def run_ours(args):
         result["e2e"] = {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                          "h2d_bytes_per_step": M * cfg["hidden"] * 2, "d2h_bytes_per_step": M * cfg["hidden"] * 2,
                          "ms_per_step": e2e_ms,
-                         "path": "pinned H2D of x and D2H of the block output inside the timed region"
+                         "path": "pinned H2D of x and D2H of the block output inside the timed region, "
+                                 "double-buffered on two copy streams under the neighbouring steps' GEMMs"
                                  + ("; each rank copies 1/N of the rows each way, x all-gathered over NCCL"
                                     if world > 1 else "")}
         if world == 1 and not args.no_extras:
