@@ -651,7 +651,9 @@ def run_ours(args):
     comp.wait_stream(s_out)
     t1.record(comp)
     torch.cuda.synchronize()
-    assert torch.equal(yh2[(args.steps - 1) % 2], y_expect), "pipelined e2e delivered a wrong block output"
+    # bit-exact on one GPU; across ranks the reductions may legitimately change order
+    assert torch.allclose(yh2[(args.steps - 1) % 2].float(), y_expect.float(), rtol=2e-2, atol=2e-2) and \
+        (world > 1 or torch.equal(yh2[(args.steps - 1) % 2], y_expect)), "pipelined e2e delivered a wrong block output"
     e2e_ms = t0.elapsed_time(t1) / args.steps
     if world > 1:
         tt = torch.tensor([e2e_ms], device=dev)
