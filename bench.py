@@ -515,11 +515,18 @@ def run_ours(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    json_out = sys.stdout
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         # NCCL's log (e.g. its version banner) goes to stderr: stdout carries only the JSON line
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        # anything native code prints on fd 1 (NCCL's version banner) goes to stderr too;
+        # the JSON line is written to the saved stdout
+        sys.stdout.flush()
+        json_fd = os.dup(1)
+        os.dup2(2, 1)
+        json_out = os.fdopen(json_fd, "w")
         dist.init_process_group("nccl", device_id=dev)
     cfg = dict(FLUX)
     M, gs, bits = cfg["M"], cfg["gs"], cfg["bits"]
@@ -698,7 +705,7 @@ def run_ours(args):
                 result["decode_gemv"][f"M{m}"] = {"value": d["value"], "unit": "GB/s", "ms_per_step": d["ms_per_step"],
                                                   "frac_of_hbm": d["value"] / peaks["hbm_gbs"]}
             result["other_configs"] = other_configs(dev)
-        print(json.dumps(result), flush=True)
+        print(json.dumps(result), file=json_out, flush=True)
     if world > 1:
         dist.destroy_process_group()
 
