@@ -1,19 +1,22 @@
 """One quantized_matmul shape, timed with CUDA events (also the small case used for ncu
 captures).  Usage:
 
-    python -m qlinear.bench_case M N K BITS [ACT|none] [REPS] [KERNEL]
+    python bench_case.py M N K BITS [ACT|none] [REPS] [KERNEL]
 
 ACT: none, gelu_tanh, gelu or swiglu (a second W of the same shape as the up projection).
 KERNEL: auto, gemm, gemm2, gemv, gemv_tc, gemv_tma, gemv_regs or generic.
 
-(run with mlx-gen_b200 on PYTHONPATH).  Prints time per call and TFLOP/s / GB/s.
+Prints time per call and TFLOP/s / GB/s.
 Weights ~N(0, 0.02) bf16 quantized on the device (group 64), x ~N(0, 1), bias ~N(0, 0.02).
 """
+import os
 import sys
 
-import torch
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "mlx-gen_b200"))
 
-import qlinear
+import torch  # noqa: E402
+
+import qlinear  # noqa: E402
 
 
 def main(argv):

@@ -15,7 +15,8 @@
  *     & (2^bits-1); scales / biases are [N, K/group_size]; w = code*scale + bias.
  *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are
  *     asynchronous, hold no global mutable state and may run concurrently on
- *     different streams.
+ *     different streams -- except ql_quantized_matmul_noalloc, whose LoRA calls share
+ *     one fixed device array (see its declaration).
  *   - Return value is a ql_status.  On failure, ql_last_error() returns a
  *     thread-local message.  No call aborts or exits.
  */
@@ -79,7 +80,7 @@ typedef struct {
     const void *biases_up;
     const void *bias_up;       /* [N] or NULL                                          */
     /* LoRA residual: y += lora_scale * (x . A) . B with A [K, rank], B [rank, N] in
-     * x's dtype.  rank % 8 == 0.  Needs `workspace` of ql_matmul_workspace_size(). */
+     * x's dtype, any rank in [1, 4096].  Needs `workspace` of ql_matmul_workspace_size(). */
     const void *lora_a;
     const void *lora_b;
     int64_t lora_rank;
@@ -164,7 +165,7 @@ size_t ql_matmul_workspace_size(int64_t M, int64_t N, int64_t K, const ql_epilog
  * runtimes whose memory is fully reserved).  No counterpart in the reference.
  * The LoRA workspace comes from a fixed 8 MiB device array inside the library
  * (ep->workspace is ignored); a request above that (M * round_up(rank, 64) * 2
- * bytes) returns QL_EUNSUPPORTED.  The first call on a device looks up the array
+ * bytes) returns QL_EUNSUPPORTED.  The first call on a device (LoRA or not) looks up the array
  * with that device current -- make it before any stream capture.  Calls share the
  * array: calls that overlap on the GPU race.  Allocates nothing. */
 int ql_quantized_matmul_noalloc(const void *x, int x_dtype, int64_t M, int64_t K,

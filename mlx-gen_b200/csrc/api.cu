@@ -238,11 +238,3 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
 
 }  // extern "C"
 
-#ifdef QL_TRACE_TL
-// Developer build only: copies the launch timeline (TL_N records) and its launch count.
-extern "C" int ql_debug_timeline(void *out, size_t bytes, unsigned *count) {
-    if (bytes < sizeof(ql::g_tl)) return -1;
-    if (cudaMemcpyFromSymbol(out, ql::g_tl, sizeof(ql::g_tl)) != cudaSuccess) return -2;
-    return cudaMemcpyFromSymbol(count, ql::g_tl_seq, sizeof(unsigned)) == cudaSuccess ? 0 : -3;
-}
-#endif

@@ -13,9 +13,9 @@
 //     must fit (e.g. M = 32768 tokens at rank <= 128).  Larger requests are rejected
 //     with QL_EUNSUPPORTED and a message; nothing runs.
 //   * Every GPU that loads the library holds the 8 MiB until the process exits.
-//   * The first call on a device looks up the array's device address
-//     (cudaGetSymbolAddress) with that device current; make that first call before
-//     any stream capture.
+//   * The first call on a device (with or without a LoRA residual) looks up the
+//     array's device address (cudaGetSymbolAddress) with that device current; make
+//     that first call before any stream capture.
 //   * All calls on a device share the one array.  The LoRA pre-pass overwrites every
 //     byte it later reads, so no clearing is needed between calls, but two calls whose
 //     kernels overlap on the GPU (different streams, no ordering) race on it.
@@ -64,9 +64,12 @@ extern "C" int ql_quantized_matmul_noalloc(const void *x, int x_dtype, int64_t M
                     "ql_quantized_matmul_noalloc: LoRA workspace of %zu bytes exceeds the fixed %zu-byte "
                     "scratch (M * round_up(rank, 64) * 2)",
                     need, kNoAllocScratchBytes);
+    // The lookup runs on every call (cached per device), so the first call on a device
+    // does it whatever its epilogue: a warm-up call without LoRA before stream capture
+    // is enough.
+    void *scratch = nullptr;
+    if (int rc = noalloc_scratch(&scratch)) return rc;
     if (need > 0) {
-        void *scratch = nullptr;
-        if (int rc = noalloc_scratch(&scratch)) return rc;
         e.workspace = scratch;
         e.workspace_bytes = kNoAllocScratchBytes;
     }

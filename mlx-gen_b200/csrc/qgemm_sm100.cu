@@ -36,20 +36,7 @@ namespace ql {
 
 namespace gemm {
 
-#ifdef QL_TRACE
-// Developer instrumentation (built only with -DQL_TRACE): per-CTA cycle counters of each
-// role's waits, read back with ql_debug_trace().
-__device__ unsigned long long g_trace[16][160];
-#define TR_WAIT(slot, expr)                                                   \
-    ({                                                                        \
-        const long long _t0 = clock64();                                      \
-        const bool _ok = (expr);                                              \
-        if (lane == 0) atomicAdd(&g_trace[slot][blockIdx.x % 160], clock64() - _t0); \
-        _ok;                                                                  \
-    })
-#else
-#define TR_WAIT(slot, expr) (expr)
-#endif
+#define expr (expr)
 #ifndef QL_SB_AHEAD
 #define QL_SB_AHEAD 3
 #endif
@@ -186,9 +173,6 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
     else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-#ifdef QL_TRACE
-    if (threadIdx.x == 32) g_trace[7][blockIdx.x % 160] -= clock64();
-#endif
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
@@ -199,32 +183,24 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                 const int xrow = tt * BT + (int)rank * C::XROWS;
                 for (int kt = 0; kt < KT; ++kt, ++it) {
                     const int s = it % STAGES;
-                    if (!TR_WAIT(0, mbar_wait<CG == 2>(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY,
-                                   peer_abort)))
+                    if (!mbar_wait<CG == 2>(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY,
+                                   peer_abort))
                         break;
                     if (it >= (uint32_t)STAGES) {  // the MMAs that read this x stage are done
                         const uint32_t i = it - STAGES;
-                        if (!TR_WAIT(0, mbar_wait<CG == 2>(&kdone[i % KR], (i / KR) & 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY,
-                                                           peer_abort)))
+                        if (!mbar_wait<CG == 2>(&kdone[i % KR], (i / KR) & 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY,
+                                                           peer_abort))
                             break;
                     }
                     uint8_t *xs = smem + C::SMEM_X + s * C::X_STAGE_BYTES;
                     uint8_t *ws = smem + C::SMEM_W + s * C::W_STAGE_BYTES;
                     const bool wstep = kt < p.ktw;
                     // x half (or LoRA T half): counted on the leader's xfull[s]
-#ifdef QL_EXP_NOX
-                    if (rank == 0) mbar_arrive(&xfull[s]);
-#else
                     if (rank == 0) mbar_arrive_expect_tx(&xfull[s], CG * C::X_STAGE_BYTES);
-#endif
                     const CUtensorMap *xm = wstep ? &tm_x : &tm_t;
                     const int xk = wstep ? kt * BK : (kt - p.ktw) * BK;
-#ifdef QL_EXP_NOX
-                    (void)xm; (void)xk; (void)xrow; (void)xs;
-#else
                     if (CG == 2) tma_load_2d_pair(xs, xm, leader(&xfull[s]), xk, xrow);
                     else tma_load_2d(xs, xm, &xfull[s], xk, xrow);
-#endif
                     // packed W rows of this CTA: counted on the local wfull[s]
                     if (wstep) {
                         mbar_arrive_expect_tx(&wfull[s], C::W_STAGE_BYTES + C::D_STAGE_BYTES);
@@ -250,13 +226,13 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
             constexpr uint32_t idesc = umma_idesc_bf16(BW * CG, BT);
             uint32_t it = 0, tcount = 0;
             for (int tile = cid; tile < num_tiles && !*abort_flag; tile += ncl, ++tcount) {
-                if (!TR_WAIT(1, mbar_wait<CG == 2>(accempty, (tcount & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_ACC, peer_abort))) break;
+                if (!mbar_wait<CG == 2>(accempty, (tcount & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_ACC, peer_abort)) break;
                 tc_fence_after();
                 bool ok = true;
                 for (int kt = 0; kt < KT; ++kt, ++it) {
                     const int s = it % STAGES, j = it % AST;
-                    if (!TR_WAIT(2, mbar_wait<CG == 2>(&xfull[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort)) ||
-                        !TR_WAIT(3, mbar_wait<CG == 2>(&afull[j], (it / AST) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort))) {
+                    if (!mbar_wait<CG == 2>(&xfull[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort) ||
+                        !mbar_wait<CG == 2>(&afull[j], (it / AST) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort)) {
                         ok = false;
                         break;
                     }
@@ -314,7 +290,7 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
             }
             const bool has_bias = bp != nullptr;
             const float bias = (has_bias && n < p.N) ? __bfloat162float(bp[n]) : 0.f;
-            if (!TR_WAIT(warp == 4 ? 4 : 15, mbar_wait<CG == 2>(accfull, tcount & 1, abort_flag, DEV_ERR_TIMEOUT_ACC, peer_abort))) break;
+            if (!mbar_wait<CG == 2>(accfull, tcount & 1, abort_flag, DEV_ERR_TIMEOUT_ACC, peer_abort)) break;
             tc_fence_after();
 #pragma unroll 1
             for (int c = 0; c < BT / 32; ++c) {
@@ -454,19 +430,12 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
             load_sb(it + 2u * AHEAD, sb_next);
             const int lt = (int)(it / (uint32_t)KT), kt = (int)(it - (uint32_t)lt * KT);
             const int s = it % STAGES, j = it % AST;
-            if (!TR_WAIT(warp == 8 ? 5 : 15, mbar_wait<CG == 2>(&wfull[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort)) ||
+            if (!mbar_wait<CG == 2>(&wfull[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort) ||
                 (it >= (uint32_t)AST &&  // the MMAs of step it - AST released this A slot
-                 !TR_WAIT(warp == 8 ? 6 : 15, mbar_wait<CG == 2>(&kdone[(it - AST) % KR], ((it - AST) / KR) & 1, abort_flag,
-                                                                 DEV_ERR_TIMEOUT_EMPTY, peer_abort))))
+                 !mbar_wait<CG == 2>(&kdone[(it - AST) % KR], ((it - AST) / KR) & 1, abort_flag,
+                                                                 DEV_ERR_TIMEOUT_EMPTY, peer_abort)))
                 break;
             uint32_t r[32];
-#ifdef QL_EXP_NODQ
-            if (kt < p.ktw) {
-                const uint32_t *wr = reinterpret_cast<const uint32_t *>(smem + C::SMEM_W + s * C::W_STAGE_BYTES + row * C::W_ROW_BYTES);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) r[i] = wr[i % (C::W_ROW_BYTES / 4)] ^ sb[i & 3];
-            } else
-#endif
             if (kt < p.ktw) {
                 const uint32_t s0 = sb[0] * 0x10001u, b0 = sb[1] * 0x10001u;  // bf16x2 broadcast
                 const uint32_t s1 = sb[2] * 0x10001u, b1 = sb[3] * 0x10001u;
@@ -532,12 +501,8 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                     }
                 }
             }
-#ifndef QL_EXP_NOWST
             tmem_st32(taddr_lane + j * 32, r);
             tmem_st_wait();
-#else
-            if (r[0] == 0x12345u && r[31] == 7u) tmem_st32(taddr_lane + j * 32, r);
-#endif
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -554,9 +519,6 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
         }
     }
 
-#ifdef QL_TRACE
-    if (threadIdx.x == 32) g_trace[7][blockIdx.x % 160] += clock64();  // kernel span of warp 1
-#endif
     tc_fence_before();
     // no CTA of a pair may exit while its peer can still signal its barriers
     if (CG == 2) cluster_sync_all();
@@ -604,16 +566,21 @@ typedef CUresult (*PFN_encodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32
                                     const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
                                     CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// The driver entry point, resolved once (a function-local static: thread-safe
+// initialisation; a failed lookup is retried on the next call).
 static PFN_encodeTiled get_encode() {
-    static PFN_encodeTiled fn = nullptr;
-    if (!fn) {
+    static std::atomic<PFN_encodeTiled> fn{nullptr};
+    PFN_encodeTiled f = fn.load(std::memory_order_acquire);
+    if (!f) {
         void *ptr = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_encodeTiled>(ptr);
+            q == cudaDriverEntryPointSuccess) {
+            f = reinterpret_cast<PFN_encodeTiled>(ptr);
+            fn.store(f, std::memory_order_release);
+        }
     }
-    return fn;
+    return f;
 }
 
 static int make_map_2d(CUtensorMap *map, CUtensorMapDataType dt, int elem_bytes, const void *base,
@@ -708,11 +675,6 @@ static int launch_lokr(const CUtensorMap &mx, const CUtensorMap &mw, const CUten
 
 }  // namespace gemm
 
-#ifdef QL_TRACE
-extern "C" int ql_debug_trace(unsigned long long *out, int) {
-    return (int)cudaMemcpyFromSymbol(out, gemm::g_trace, sizeof(gemm::g_trace));
-}
-#endif
 
 // x [M,K] bf16, W packed [N,K] (+ W3 for SwiGLU), scales/biases bf16.
 // lora_t: [M, r_pad] bf16 (r_pad = round_up(rank, 64)) already holding s.(x.A), or null.

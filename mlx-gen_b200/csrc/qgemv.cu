@@ -132,7 +132,6 @@ __global__ void __launch_bounds__(WARPS * 32, 2) qgemv_kernel(const Params p) {
     extern __shared__ __align__(16) uint16_t xs[];
     __shared__ float red[NPASS][WARPS][16][8];
 
-    TL_T(tl_entry);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
     const int nstrips = (p.N + 15) / 16;
@@ -159,7 +158,6 @@ __global__ void __launch_bounds__(WARPS * 32, 2) qgemv_kernel(const Params p) {
     }
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    TL_T(tl_wait);
 
     // x -> shared memory (permuted, see xs_index)
     for (int e = threadIdx.x * 8; e < p.M * p.K; e += WARPS * 32 * 8) {
@@ -272,7 +270,6 @@ __global__ void __launch_bounds__(WARPS * 32, 2) qgemv_kernel(const Params p) {
         }
         __syncthreads();
     }
-    if (threadIdx.x == 0) TL_RECORD(SWIGLU ? 3 : 2, tl_entry, tl_wait);
 }
 
 }  // namespace gemv

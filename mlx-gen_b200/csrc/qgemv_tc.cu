@@ -44,9 +44,6 @@
 
 namespace ql {
 namespace gemv3 {
-#ifdef QL_TRACE
-using gemm::g_trace;
-#endif
 
 constexpr int ROWS = 128;     // weight rows per tile (MMA M)
 constexpr int STAGES = 3;     // weight stages of 128 rows x 256 bytes
@@ -174,9 +171,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     float2 *ginfo = reinterpret_cast<float2 *>(red + (p.split - 1) * ROWS * 8); // [groups][8] (s-scale, sum x)
     float *kscale = reinterpret_cast<float *>(ginfo + p.sps * GPS * 8);         // [groups][8] 2^k
 
-#ifdef QL_TRACE
-    const long long t_entry = clock64();
-#endif
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rank = p.split > 1 ? (int)cluster_ctarank() : 0;
     const int cluster = blockIdx.x / p.split, nclusters = gridDim.x / p.split;
@@ -219,12 +213,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tmem_alloc(tmem_slot, TMEM_COLS);
         tc_fence_before();
     }
-#ifdef QL_TRACE
-    if (threadIdx.x == 32) {
-        g_trace[9][blockIdx.x % 160] -= clock64();
-        g_trace[10][blockIdx.x % 160] += clock64() - t_entry;
-    }
-#endif
 
     if (warp >= 2) {
         // ---------------------------------------------- activations -> e4m3 pieces in smem
@@ -306,9 +294,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (warp >= 1) named_bar_sync(1, NTHREADS - 32);  // warps 1-15: pieces, group info and TMEM ready
     tc_fence_after();
     const uint32_t tmem = warp >= 1 ? *tmem_slot : 0u;
-#ifdef QL_TRACE
-    if (threadIdx.x == 32) g_trace[12][blockIdx.x % 160] += clock64() - t_entry;
-#endif
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
@@ -321,8 +306,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     for (int g8 = st * GPS; g8 < (st + 1) * GPS; g8 += 8) {
                         if (g8 % 8) continue;  // GPS < 8: the batch started in an earlier stage
                         const int b = sbc % SBR;
-                        if (!TR_WAIT(1, mbar_wait(&sbempty[b], ((sbc / SBR) & 1) ^ 1, abort_flag,
-                                                  DEV_ERR_TIMEOUT_EMPTY))) {
+                        if (!mbar_wait(&sbempty[b], ((sbc / SBR) & 1) ^ 1, abort_flag,
+                                                  DEV_ERR_TIMEOUT_EMPTY)) {
                             ok = false;
                             break;
                         }
@@ -338,7 +323,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                     if (!ok) break;
                     const int s = it % STAGES;
-                    if (!TR_WAIT(0, mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY))) {
+                    if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY)) {
                         ok = false;
                         break;
                     }
@@ -363,17 +348,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int upt = nst * UPS;  // units per tile
             uint32_t u = 0;
             bool ok = true;
-#ifdef QL_EXP_PRODONLY
-            ok = false;
-#endif
             for (int tile = cluster; tile < p.ntiles && ok; tile += nclusters) {
 #pragma unroll 1
                 for (int uu = 0; uu < upt; ++uu, ++u) {
                     if ((int)(u % NISSUE) != warp - 1) continue;
                     const int us = u % AU;
                     const uint32_t ph = (u / AU) & 1;
-                    if (!TR_WAIT(3, mbar_wait(&afull[us], ph, abort_flag, DEV_ERR_TIMEOUT_FULL)) ||
-                        !TR_WAIT(4, mbar_wait(&dfree[us], ph ^ 1, abort_flag, DEV_ERR_TIMEOUT_ACC))) {
+                    if (!mbar_wait(&afull[us], ph, abort_flag, DEV_ERR_TIMEOUT_FULL) ||
+                        !mbar_wait(&dfree[us], ph ^ 1, abort_flag, DEV_ERR_TIMEOUT_ACC)) {
                         ok = false;
                         break;
                     }
@@ -383,11 +365,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     for (int ks = 0; ks < KPU; ++ks) {
                         const int c = uu * UCH + ks / 4;  // chunk of the slice = 128-K block of B
                         const uint64_t bdesc = umma_desc_k_sw128(bxs + c * 2048) + 2 * (ks % 4);
-#ifndef QL_EXP_NOMMA
                         tc_mma_ts_f8(dbase + (ks / KPG) * 16, abase + ks * 8, bdesc, idesc, (ks % KPG) ? 1u : 0u);
-#else
-                        (void)bdesc; (void)dbase; (void)abase;
-#endif
                     }
                     tc_commit(&udone[us]);
                 }
@@ -402,16 +380,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int tile = cluster; tile < p.ntiles && ok; tile += nclusters) {
             for (int st = st0; st < st1 && ok; ++st, ++it) {
                 const int s = it % STAGES;
-                if (!TR_WAIT(warp == 4 ? 5 : 15, mbar_wait(&full[s], (it / STAGES) & 1, abort_flag,
-                                                           DEV_ERR_TIMEOUT_FULL))) {
+                if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag,
+                                                           DEV_ERR_TIMEOUT_FULL)) {
                     ok = false;
                     break;
                 }
-#ifdef QL_EXP_PRODONLY
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
-                continue;
-#endif
                 const uint8_t *wrow = smem + s * W_BYTES + row * 128;
                 // the loads of unit j + 1 are issued while unit j's TMEM store is in flight
                 uint4 wv[4 * UCH];
@@ -430,13 +403,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int j = 0; j < UPS; ++j, ++u) {
                     const int us = u % AU;
-                    if (!TR_WAIT(warp == 4 ? 6 : 15, mbar_wait(&udone[us], ((u / AU) & 1) ^ 1, abort_flag,
-                                                               DEV_ERR_TIMEOUT_EMPTY))) {
+                    if (!mbar_wait(&udone[us], ((u / AU) & 1) ^ 1, abort_flag,
+                                                               DEV_ERR_TIMEOUT_EMPTY)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-#ifndef QL_EXP_NODQ
 #pragma unroll
                     for (int ch = 0; ch < UCH; ++ch) {
                         uint32_t r[32];
@@ -452,9 +424,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         }
                         tmem_st32(taddr + us * 32 * UCH + ch * 32, r);
                     }
-#else
-                    if (wv[0].x == 0x12345678u && wv[1].y == 0x9abcdef0u) mbar_arrive(&afull[us]);  // keep the loads
-#endif
                     if (j + 1 < UPS) {
                         load_unit(j + 1);
                     } else {
@@ -483,32 +452,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll 1
             for (int ub = 0; ub < upt && ok; ub += upb, ++sbc) {
                 const int b = sbc % SBR;
-                if (!TR_WAIT(warp == 8 ? 7 : 15, mbar_wait(&sbfull[b], (sbc / SBR) & 1, abort_flag,
-                                                           DEV_ERR_TIMEOUT_FULL))) {
+                if (!mbar_wait(&sbfull[b], (sbc / SBR) & 1, abort_flag,
+                                                           DEV_ERR_TIMEOUT_FULL)) {
                     ok = false;
                     break;
                 }
                 const uint8_t *sp = sb_ring + b * SB_SLOT;
-#ifdef QL_EXP_PRODONLY
-                u += upb;
-                mbar_arrive(&sbempty[b]);
-                continue;
-#endif
 #pragma unroll 1
                 for (int uu = ub + fset; uu < ub + upb; uu += 2) {
                     const uint32_t uc = u + (uu - ub);  // unit counter of this unit
                     const int us = uc % AU;
-                    if (!TR_WAIT(warp == 8 ? 8 : 15, mbar_wait(&udone[us], (uc / AU) & 1, abort_flag,
-                                                               DEV_ERR_TIMEOUT_ACC))) {
+                    if (!mbar_wait(&udone[us], (uc / AU) & 1, abort_flag,
+                                                               DEV_ERR_TIMEOUT_ACC)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     uint32_t v[16 * GPUN];
-#ifdef QL_EXP_NOFOLD
-                    if (lane == 0) mbar_arrive(&dfree[us]);
-                    continue;
-#endif
                     if (GPUN == 2)
                         tmem_ld32(taddr + us * 32, v);
                     else
@@ -576,7 +536,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     mbar_arrive_cluster(mapa_shared(smem_u32(redfull), 0));
                     continue;
                 }
-                if (!TR_WAIT(warp == 8 ? 11 : 15, mbar_wait<true>(redfull, tc & 1, abort_flag, DEV_ERR_TIMEOUT_ACC))) {
+                if (!mbar_wait<true>(redfull, tc & 1, abort_flag, DEV_ERR_TIMEOUT_ACC)) {
                     ok = false;
                     break;
                 }
@@ -644,12 +604,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     }
 
-#ifdef QL_TRACE
-    if (threadIdx.x == 32) {
-        g_trace[9][blockIdx.x % 160] += clock64();
-        g_trace[13][blockIdx.x % 160] += clock64() - t_entry;
-    }
-#endif
     tc_fence_before();
     __syncthreads();
     if (p.split > 1) cluster_sync_all();  // no CTA leaves while a peer may still write to it

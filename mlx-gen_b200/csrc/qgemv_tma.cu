@@ -54,9 +54,6 @@ struct Cfg {
 
 __device__ __forceinline__ void mma16816(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-#ifdef QL_EXP_NOMMA
-    d[0] += __uint_as_float(a0 ^ a1 ^ b0); d[1] += __uint_as_float(a2 ^ a3 ^ b1); return;
-#endif
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
         "{%8, %9}, {%0, %1, %2, %3};"
@@ -66,9 +63,6 @@ __device__ __forceinline__ void mma16816(float d[4], uint32_t a0, uint32_t a1, u
 
 // bf16x2 (128 + code_lo, 128 + code_hi) from the nibbles at bit 4j and 16 + 4j
 __device__ __forceinline__ uint32_t nib2(uint32_t w, int j) {
-#ifdef QL_EXP_NONIB
-    return w + j;
-#endif
     return ((w >> (4 * j)) & 0x000f000fu) | 0x43004300u;
 }
 
@@ -78,7 +72,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                      const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_w2,
                      const __grid_constant__ CUtensorMap tm_s2, const __grid_constant__ CUtensorMap tm_b2,
                      const Params p) {
-    TL_T(tl_entry);
     using C = Cfg<BITS, SWIGLU>;
     constexpr int NPASS = C::NPASS, STAGES = C::STAGES;
     constexpr int GPS = KS / GS;                            // groups per stage
@@ -142,7 +135,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
 
     // -------------------------------------------------------------------- consumers
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    TL_T(tl_wait);
     const int tid = threadIdx.x;  // consumer thread, 0 .. CWARPS * 32 - 1
     // x -> smem, permuted so that lane c of a warp reads its four bf16 pairs of a run in
     // one 16-byte load: Q4 pairs (0,4) (1,5) (2,6) (3,7), Q8 pairs (0,2) (1,3) (4,6) (5,7)
@@ -200,11 +192,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                 break;
             }
             const uint8_t *sp = stages + s * STAGE_BYTES;
-#ifdef QL_EXP_NOCOMP
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            continue;
-#endif
             // ---- load phase: everything this warp needs from the stage goes to registers,
             //      then the stage is released so the producer can refill it at once
             constexpr int NG = 128 / GS;                 // groups covered by this warp's 4 runs
@@ -254,11 +241,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
-#ifdef QL_EXP_LOADONLY
-#pragma unroll
-            for (int rr = 0; rr < 4; ++rr) acc[0][0] += __uint_as_float(wgv[0][rr][0] ^ whv[0][rr][0] ^ X[rr].x ^ sgv[0][0] ^ bhv[0][NG - 1]);
-            continue;
-#endif
             // ---- compute phase.  Every MMA of the stage first (independent accumulators:
             //      per group, per plane -- Q4 halves a/b, Q8 low/high nibbles -- and, for
             //      one group per warp, per run parity), runs of different groups interleaved;
@@ -368,10 +350,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             }
         }
     }
-#ifdef QL_TRACE_TL
-    named_bar_sync(1, CWARPS * 32);
-    if (threadIdx.x == 0) TL_RECORD(SWIGLU ? 5 : 4, tl_entry, tl_wait);
-#endif
 }
 
 static int make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, int rank, const uint64_t *dims,

@@ -231,41 +231,6 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
-#ifdef QL_TRACE_TL
-// Developer instrumentation (built only with -DQL_TRACE_TL): a launch timeline of the
-// kernels that wait on their predecessor (griddepcontrol.wait).  Per launch: earliest /
-// latest CTA entry, return from the wait and CTA end (%globaltimer ns; minima stored
-// complemented so that a zeroed record starts empty).  Read with ql_debug_timeline().
-struct TlRec {
-    unsigned long long nentry_min, entry_max, nwait_min, wait_max, nend_min, end_max;
-    unsigned kind, grid, done, pad;
-};
-constexpr int TL_N = 8192;
-__device__ TlRec g_tl[TL_N];  // the library is one translation unit (libqlinear.cu)
-__device__ unsigned g_tl_seq;
-// One thread per CTA, after the CTA's last store.  The launch index is read after the
-// CTA's griddepcontrol.wait, so every earlier traced launch has counted itself.
-__device__ __forceinline__ void tl_record(unsigned kind, uint64_t t_entry, uint64_t t_wait) {
-    const uint64_t t_end = globaltimer_ns();
-    const unsigned id = *reinterpret_cast<volatile unsigned *>(&g_tl_seq);
-    TlRec &r = g_tl[id % TL_N];
-    atomicMax(&r.nentry_min, ~(unsigned long long)t_entry);
-    atomicMax(&r.entry_max, (unsigned long long)t_entry);
-    atomicMax(&r.nwait_min, ~(unsigned long long)t_wait);
-    atomicMax(&r.wait_max, (unsigned long long)t_wait);
-    atomicMax(&r.nend_min, ~(unsigned long long)t_end);
-    atomicMax(&r.end_max, (unsigned long long)t_end);
-    r.kind = kind;
-    r.grid = gridDim.x;
-    __threadfence();
-    if (atomicAdd(&r.done, 1u) == gridDim.x - 1) atomicAdd(&g_tl_seq, 1u);
-}
-#define TL_T(var) const uint64_t var = globaltimer_ns()
-#define TL_RECORD(kind, t0, t1) tl_record(kind, t0, t1)
-#else
-#define TL_T(var)
-#define TL_RECORD(kind, t0, t1)
-#endif
 
 template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
