@@ -115,6 +115,16 @@ const char *ql_last_error(void);
  * when a bounded wait runs out.  Synchronises the current device.  0 = no error. */
 int ql_device_error(int clear);
 
+/* Test hook for the failure path (no counterpart in the reference, whose failure model is
+ * a cooperative cancel flag, gen-core/src/runtime.rs:239-258).  Every pipelined kernel's
+ * waits are bounded: when one runs out the kernel records a DEV_ERR timeout code in the
+ * device error word (read with ql_device_error), every role drains, TMEM is freed and the
+ * kernel returns; the context stays usable.  wait_limit_ns replaces the 2 s limit on the
+ * current device (0 restores it); flags bit 0 makes the tcgen05 GEMM's TMA producer issue
+ * nothing, so its consumers' waits run out.  Synchronises the current device.  Not for
+ * production use: set flags back to 0 afterwards. */
+int ql_debug_inject(unsigned flags, unsigned long long wait_limit_ns);
+
 /* Replaces mlx_rs::ops::quantize(w, group_size, bits) -> (wq, scales, biases)
  * (called at src/quant.rs:140, src/adapters.rs:533-537 via
  * QuantizedLinear::try_from_linear, src/nn.rs:91-93).  w [N, K] in w_dtype;

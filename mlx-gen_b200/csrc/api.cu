@@ -94,6 +94,15 @@ int ql_device_error(int clear) {
     return (int)v;
 }
 
+int ql_debug_inject(unsigned flags, unsigned long long wait_limit_ns) {
+    g_err[0] = 0;
+    const unsigned long long lim = wait_limit_ns ? wait_limit_ns : kWaitLimitNs;
+    QL_CUDA_TRY(cudaDeviceSynchronize());
+    QL_CUDA_TRY(cudaMemcpyToSymbol(g_wait_limit_ns, &lim, sizeof(lim)));
+    QL_CUDA_TRY(cudaMemcpyToSymbol(g_debug_inject, &flags, sizeof(flags)));
+    return QL_OK;
+}
+
 int ql_quantize(const void *w, int w_dtype, int64_t N, int64_t K, int group_size, int bits,
                 uint32_t *wq, void *scales, void *biases, int sb_dtype, void *stream) {
     g_err[0] = 0;

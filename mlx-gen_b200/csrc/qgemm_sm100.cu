@@ -37,15 +37,13 @@ namespace ql {
 namespace gemm {
 
 #define expr (expr)
-#ifndef QL_SB_AHEAD
-#define QL_SB_AHEAD 3
-#endif
 
 constexpr int BT = 256;        // tokens per tile (MMA N)
 constexpr int BW = 128;        // weight rows per CTA per tile (MMA M per CTA)
 constexpr int BK = 64;         // K per pipeline step (one 128-byte swizzle row of bf16)
 constexpr int AST = 4;         // TMEM A ring depth (32 columns each)
 constexpr int KR = 8;          // k-step completion ring (>= STAGES and AST)
+constexpr int SBR = 8;         // scale/bias ring depth (k-steps staged ahead by warp 2)
 constexpr int NTHREADS = 512;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t ACC_COL = 0;
@@ -71,8 +69,10 @@ struct Cfg {
     static constexpr int SMEM_D = SMEM_W + STAGES * W_STAGE_BYTES;    // LoKr delta tiles (1 KB aligned)
     static constexpr int SMEM_XCH = SMEM_D + STAGES * D_STAGE_BYTES;  // swiglu exchange
     static constexpr int XCH_BYTES = 64 * 33 * 4;
-    static constexpr int SMEM_BAR = SMEM_XCH + XCH_BYTES;
-    static constexpr int NBAR = 3 * STAGES + AST + KR + 2;
+    static constexpr int SMEM_SB = SMEM_XCH + XCH_BYTES;             // scale/bias ring
+    static constexpr int SB_SLOT_BYTES = BW * 8;                      // {s0 b0, s1 b1} per row
+    static constexpr int SMEM_BAR = SMEM_SB + SBR * SB_SLOT_BYTES;
+    static constexpr int NBAR = 3 * STAGES + AST + KR + 2 + 2 * SBR;
     static_assert(KR >= STAGES && KR >= AST, "k-step ring");
     static constexpr int SMEM_MISC = SMEM_BAR + NBAR * 8;
     static constexpr int SMEM_TOTAL = SMEM_MISC + 16 + 1024;  // + alignment slack
@@ -133,6 +133,9 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
     uint64_t *kdone = afull + AST;
     uint64_t *accfull = kdone + KR;         // accumulator complete
     uint64_t *accempty = accfull + 1;       // accumulator drained (leader: both CTAs' warps)
+    uint64_t *sbfull = accempty + 1;        // scale/bias slot written (warp 2, 32 lanes)
+    uint64_t *sbempty = sbfull + SBR;       // scale/bias slot read (4 dequant warps)
+    uint2 *sb_ring = reinterpret_cast<uint2 *>(smem + C::SMEM_SB);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::SMEM_MISC);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::SMEM_MISC + 4);
 
@@ -157,6 +160,10 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
         for (int j = 0; j < KR; ++j) mbar_init(&kdone[j], 1);
         mbar_init(accfull, 1);
         mbar_init(accempty, 4 * CG);
+        for (int j = 0; j < SBR; ++j) {
+            mbar_init(&sbfull[j], 32);
+            mbar_init(&sbempty[j], 4);
+        }
         *abort_flag = 0;
         mbar_fence_init();
         prefetch_tmap(&tm_x);
@@ -176,7 +183,8 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
-        if (lane == 0) {
+        // (a test can make it issue nothing, so that its consumers' bounded waits run out)
+        if (lane == 0 && !(*reinterpret_cast<volatile unsigned *>(&g_debug_inject) & 1u)) {
             uint32_t it = 0;
             for (int tile = cid; tile < num_tiles && !*abort_flag; tile += ncl) {
                 const int wt = tile % p.num_w_tiles, tt = tile / p.num_w_tiles;
@@ -375,59 +383,128 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                 }
             }
         }
+    } else if (warp == 2) {
+        // ---------------------------------------------------------------- scale/bias producer
+        // For every k-step of this CTA (flattened over its tiles, in the dequant warps'
+        // order) the warp writes a shared-memory ring slot holding, per weight row,
+        // {s(group of k0) | b << 16, s(group of k0 + 32) | b << 16}.  Lane l serves rows l,
+        // l + 32, l + 64, l + 96.  Scales and biases are read from global memory in chunks
+        // of 8 groups per row (one 16-byte load each when the rows allow it), and the next
+        // chunk's loads are in flight while the current chunk's slots are written, so
+        // their latency stays in this warp.
+        const int my_tiles = cid < num_tiles ? (num_tiles - 1 - cid) / ncl + 1 : 0;
+        const bool vec = (p.G % 8) == 0 && ((reinterpret_cast<uintptr_t>(p.scales) | reinterpret_cast<uintptr_t>(p.biases)) & 15) == 0 &&
+                         (!SWIGLU || ((reinterpret_cast<uintptr_t>(p.scales2) | reinterpret_cast<uintptr_t>(p.biases2)) & 15) == 0);
+        const int nchunk = (p.G + 7) / 8;  // chunks of 8 groups per tile
+        // chunk registers: per row r4, 8 scales (4 words) then 8 biases (4 words)
+        auto load_chunk = [&](int lt, int c, uint32_t (&o)[4][8]) {
+            const int wt = (cid + lt * ncl) % p.num_w_tiles;
+#pragma unroll
+            for (int r4 = 0; r4 < 4; ++r4) {
+                const int row = r4 * 32 + lane;
+                const uint16_t *sc, *bi;
+                int n;
+                if (SWIGLU) {
+                    sc = reinterpret_cast<const uint16_t *>(row < 64 ? p.scales : p.scales2);
+                    bi = reinterpret_cast<const uint16_t *>(row < 64 ? p.biases : p.biases2);
+                    n = (wt * CG + (int)rank) * 64 + (row & 63);
+                } else {
+                    sc = reinterpret_cast<const uint16_t *>(p.scales);
+                    bi = reinterpret_cast<const uint16_t *>(p.biases);
+                    n = (wt * CG + (int)rank) * BW + row;
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[r4][i] = 0;
+                if (n >= p.N || lt >= my_tiles) continue;
+                const int64_t base = (int64_t)n * p.G + c * 8;
+                if (vec) {
+                    const uint4 sv = __ldg(reinterpret_cast<const uint4 *>(sc + base));
+                    const uint4 bv = __ldg(reinterpret_cast<const uint4 *>(bi + base));
+                    o[r4][0] = sv.x, o[r4][1] = sv.y, o[r4][2] = sv.z, o[r4][3] = sv.w;
+                    o[r4][4] = bv.x, o[r4][5] = bv.y, o[r4][6] = bv.z, o[r4][7] = bv.w;
+                } else {
+#pragma unroll
+                    for (int g = 0; g < 8; ++g) {
+                        if (c * 8 + g < p.G) {
+                            o[r4][g >> 1] |= (uint32_t)__ldg(sc + base + g) << (16 * (g & 1));
+                            o[r4][4 + (g >> 1)] |= (uint32_t)__ldg(bi + base + g) << (16 * (g & 1));
+                        }
+                    }
+                }
+            }
+        };
+        // 16-bit entry g (0..7) of a 4-word register group
+        auto pick = [](const uint32_t *w4, int g) -> uint32_t {
+            const uint32_t lo = (g & 2) ? w4[1] : w4[0], hi = (g & 2) ? w4[3] : w4[2];
+            const uint32_t wsel = (g & 4) ? hi : lo;
+            return (g & 1) ? (wsel >> 16) : (wsel & 0xffffu);
+        };
+        uint32_t cur[4][8], nxt[4][8];
+        uint32_t it = 0;
+        bool ok = true;
+        if (nchunk > 0) load_chunk(0, 0, nxt);
+        for (int lt = 0; lt < my_tiles && ok; ++lt) {
+            for (int c = 0; c < nchunk && ok; ++c) {
+#pragma unroll
+                for (int r4 = 0; r4 < 4; ++r4)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) cur[r4][i] = nxt[r4][i];
+                // prefetch the next chunk (of this tile, or the first of the next tile)
+                if (c + 1 < nchunk) load_chunk(lt, c + 1, nxt);
+                else load_chunk(lt + 1, 0, nxt);
+                // k-steps whose first group lies in chunk c
+                const int kt0 = (c * 8 * p.gs + BK - 1) / BK;
+                const int kt1 = min(p.ktw, ((c + 1) * 8 * p.gs + BK - 1) / BK);
+                for (int kt = kt0; kt < kt1; ++kt, ++it) {
+                    const int slot = it % SBR;
+                    if (!mbar_wait<false>(&sbempty[slot], ((it / SBR) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    const int g0 = kt * BK / p.gs - c * 8, g1 = (kt * BK + 32) / p.gs - c * 8;
+#pragma unroll
+                    for (int r4 = 0; r4 < 4; ++r4) {
+                        // g1 may fall in the next chunk only when gs = 32 and the step straddles
+                        // chunks, which cannot happen (8 groups of 32 = 4 whole k-steps)
+                        const uint32_t s0 = pick(cur[r4], g0), b0 = pick(cur[r4] + 4, g0);
+                        const uint32_t s1 = pick(cur[r4], g1 & 7), b1 = pick(cur[r4] + 4, g1 & 7);
+                        sb_ring[slot * BW + r4 * 32 + lane] = make_uint2(s0 | (b0 << 16), s1 | (b1 << 16));
+                    }
+                    mbar_arrive(&sbfull[slot]);  // each lane after its own stores (count 32)
+                }
+            }
+            // LoRA k-steps of this tile: no scales (the dequant warps do not read the slot)
+            for (int kt = p.ktw; kt < KT && ok; ++kt, ++it) {
+                const int slot = it % SBR;
+                if (!mbar_wait<false>(&sbempty[slot], ((it / SBR) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive(&sbfull[slot]);
+            }
+        }
     } else if (warp >= 8) {
         // ---------------------------------------------------------------- dequant warpgroups
         // Warpgroup wg handles this CTA's k-steps it = wg, wg + 2, ... (flattened over
-        // tiles).  The scales / biases of step it+2 are loaded before step it is
-        // processed, so their L2 latency stays off the critical path.
+        // tiles); the scales / biases of each step come from warp 2's ring.
         const int wg = (warp - 8) >> 2, q = warp & 3;
         const int row = q * 32 + lane;
         const uint32_t taddr_lane = tmem + ((uint32_t)(q * 32) << 16) + A_COL;
         const int my_tiles = cid < num_tiles ? (num_tiles - 1 - cid) / ncl + 1 : 0;
         const uint32_t total = (uint32_t)my_tiles * (uint32_t)KT;
 
-        // weight row (global) of this thread for tile `tile`, plus its scale/bias arrays
-        auto row_of = [&](int tile, const uint16_t *&sc, const uint16_t *&bi) -> int {
+        // weight row (global) of this thread for tile `tile` (LoRA steps)
+        auto row_n = [&](int tile) -> int {
             const int wt = tile % p.num_w_tiles;
-            if (SWIGLU) {
-                sc = reinterpret_cast<const uint16_t *>(row < 64 ? p.scales : p.scales2);
-                bi = reinterpret_cast<const uint16_t *>(row < 64 ? p.biases : p.biases2);
-                return (wt * CG + (int)rank) * 64 + (row & 63);
-            }
-            sc = reinterpret_cast<const uint16_t *>(p.scales);
-            bi = reinterpret_cast<const uint16_t *>(p.biases);
-            return (wt * CG + (int)rank) * BW + row;
+            return SWIGLU ? (wt * CG + (int)rank) * 64 + (row & 63) : (wt * CG + (int)rank) * BW + row;
         };
-        // scale/bias bf16 bits of step `it`: {s(group of k0), b(..), s(group of k0+32), b(..)}
-        auto load_sb = [&](uint32_t it, uint32_t out[4]) {
-            out[0] = out[1] = out[2] = out[3] = 0;
-            if (it >= total) return;
-            const int lt = (int)(it / (uint32_t)KT), kt = (int)(it - (uint32_t)lt * KT);
-            if (kt >= p.ktw) return;
-            const uint16_t *sc, *bi;
-            const int n = row_of(cid + lt * ncl, sc, bi);
-            if (n >= p.N) return;
-            const int g0 = kt * BK / p.gs, g1 = (kt * BK + 32) / p.gs;
-            const int64_t base = (int64_t)n * p.G;
-            if (g0 < p.G) {
-                out[0] = __ldg(sc + base + g0);
-                out[1] = __ldg(bi + base + g0);
-            }
-            if (g1 < p.G) {
-                out[2] = __ldg(sc + base + g1);
-                out[3] = __ldg(bi + base + g1);
-            }
-        };
-        // scales/biases are loaded QL_SB_AHEAD of this warpgroup's steps ahead of use
-        constexpr int AHEAD = QL_SB_AHEAD;
-        uint32_t sbq[AHEAD][4];
-#pragma unroll
-        for (int a = 0; a < AHEAD; ++a) load_sb((uint32_t)wg + 2u * a, sbq[a]);
         for (uint32_t it = (uint32_t)wg; it < total; it += 2) {
-            uint32_t sb[4], sb_next[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) sb[i] = sbq[0][i];
-            load_sb(it + 2u * AHEAD, sb_next);
+            const int slot = it % SBR;
+            if (!mbar_wait<false>(&sbfull[slot], (it / SBR) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL)) break;
+            const uint2 sbv = sb_ring[slot * BW + row];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sbempty[slot]);
+            const uint32_t sb[4] = {sbv.x & 0xffffu, sbv.x >> 16, sbv.y & 0xffffu, sbv.y >> 16};
             const int lt = (int)(it / (uint32_t)KT), kt = (int)(it - (uint32_t)lt * KT);
             const int s = it % STAGES, j = it % AST;
             if (!mbar_wait<CG == 2>(&wfull[s], (it / STAGES) & 1, abort_flag, DEV_ERR_TIMEOUT_FULL, peer_abort) ||
@@ -439,10 +516,15 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
             if (kt < p.ktw) {
                 const uint32_t s0 = sb[0] * 0x10001u, b0 = sb[1] * 0x10001u;  // bf16x2 broadcast
                 const uint32_t s1 = sb[2] * 0x10001u, b1 = sb[3] * 0x10001u;
-                const uint8_t *wrow = smem + C::SMEM_W + s * C::W_STAGE_BYTES + row * C::W_ROW_BYTES;
+                // The packed rows arrive 32-byte (Q4) / 64-byte (Q8) swizzled: 16-byte chunk h of
+                // row r sits at chunk h ^ ((r >> 2) & 1) (Q4) / h ^ ((r >> 1) & 3) (Q8), so the
+                // eight rows a quarter-warp reads hit eight different bank groups.
+                const uint4 *wrow = reinterpret_cast<const uint4 *>(smem + C::SMEM_W + s * C::W_STAGE_BYTES +
+                                                                    row * C::W_ROW_BYTES);
                 if constexpr (BITS == 4) {
-                    uint4 a = reinterpret_cast<const uint4 *>(wrow)[0];
-                    uint4 b = reinterpret_cast<const uint4 *>(wrow)[1];
+                    const int sw = (row >> 2) & 1;
+                    uint4 a = wrow[sw];
+                    uint4 b = wrow[sw ^ 1];
                     const uint32_t wv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
@@ -456,7 +538,7 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                     const float fs0 = bf16lo(s0), fb0 = bf16lo(b0), fs1 = bf16lo(s1), fb1 = bf16lo(b1);
 #pragma unroll
                     for (int h = 0; h < 4; ++h) {
-                        uint4 a = reinterpret_cast<const uint4 *>(wrow)[h];
+                        uint4 a = wrow[h ^ ((row >> 1) & 3)];
                         const uint32_t wv[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
@@ -473,8 +555,7 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                 }
             } else {
                 // LoRA step: A = B^T rows for this tile, columns [64l, 64l + 64) of rank.
-                const uint16_t *sc, *bi;
-                const int n = row_of(cid + lt * ncl, sc, bi);
+                const int n = row_n(cid + lt * ncl);
                 const bool row_ok = n < p.N;
                 const int l0 = (kt - p.ktw) * BK;
 #pragma unroll
@@ -510,12 +591,6 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                 else mbar_arrive(&afull[j]);
                 mbar_arrive(&empty[s]);
             }
-#pragma unroll
-            for (int a = 0; a + 1 < AHEAD; ++a)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) sbq[a][i] = sbq[a + 1][i];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) sbq[AHEAD - 1][i] = sb_next[i];
         }
     }
 
@@ -732,13 +807,16 @@ int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, 
     const uint64_t words = (uint64_t)K * bits / 32;
     const uint32_t box_words = (uint32_t)(BK * bits / 32);
     const uint32_t box_rows = swiglu ? 64 : BW;
+    // rows of 32 B (Q4) / 64 B (Q8) per k-step, swizzled so that the dequant warps' reads
+    // are free of bank conflicts
+    const CUtensorMapSwizzle wsw = bits == 4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
     rc = make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wq, words, (uint64_t)N, words * 4, box_words,
-                     box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+                     box_rows, wsw);
     if (rc) return rc;
     mw2 = mw;
     if (swiglu) {
         rc = make_map_2d(&mw2, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wq2, words, (uint64_t)N, words * 4,
-                         box_words, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+                         box_words, box_rows, wsw);
         if (rc) return rc;
     }
     mt = mx;

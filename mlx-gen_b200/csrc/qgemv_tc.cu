@@ -238,7 +238,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
             }
             const int ea = (int)((__float_as_uint(amax) >> 23) & 0xff) - 127;
-            const int k = max(-100, min(100, KTOP - ea));
+            // 2^k and 2^(9-k) must both be normal floats: k in [-118, 127] (a subnormal
+            // group max gives ea = -127 and the largest scale, 2^127)
+            const int k = max(-118, min(127, KTOP - ea));
             kscale[i] = __int_as_float((k + 127) << 23);
             ginfo[i] = make_float2(__int_as_float((9 - k + 127) << 23), sum);
         }
@@ -280,7 +282,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
                             v[8 * h + q] = xs[4 * h + q] * sc;
-                            v[8 * h + 4 + q] = xs[4 * h + q] * (16.f * sc);
+                            v[8 * h + 4 + q] = (xs[4 * h + q] * sc) * 16.f;  // sc may be 2^127
                         }
                 }
                 split_pieces(v, hi, lo);

@@ -224,6 +224,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // exit instead of hanging the GPU.  Waits also give up as soon as another role
 // has aborted.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// The limit in force (kWaitLimitNs unless a test shortened it through ql_debug_inject), and
+// the test hook's injection flags (bit 0: the tcgen05 GEMM's TMA producer issues nothing).
+__device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
+__device__ unsigned g_debug_inject = 0;
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
@@ -241,7 +245,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
         if (mbar_try_wait<CLUSTER>(bar, parity)) return true;
         if ((i & 63u) == 0) {
             if (*abort) return false;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (globaltimer_ns() - t0 > *reinterpret_cast<volatile unsigned long long *>(&g_wait_limit_ns)) {
                 raise_dev_error(code);
                 *abort = 1;
                 // peer_abort: shared::cluster address of the paired CTA's abort flag

@@ -11,7 +11,7 @@ from ._lib import (ACT_GELU_ERF, ACT_GELU_TANH, ACT_NONE, ACT_SWIGLU, KERNEL_AUT
 from .nn import (DEFAULT_GROUP_SIZE, AdaptableLinear, Linear, Lokr, Lora, QuantizedLinear,
                  TokenEmbedding)
 from .ops import dequantize, dequantize_rows, layernorm_modulate, quantize, quantized_matmul, workspace_size
-from .quant import embedding, lin, packed_bits, quantize_map
+from .quant import PackedShapeError, embedding, lin, packed_bits, quantize_map
 from .adapters import reconstruct_loha_delta, reconstruct_lokr_delta, reconstruct_lokr_delta_scaled
 
 __all__ = [
@@ -19,6 +19,6 @@ __all__ = [
     "KERNEL_GEMV", "KERNEL_GEMV_REGS", "KERNEL_GEMV_TC", "KERNEL_GEMV_TMA", "KERNEL_GENERIC", "QlError", "device_error", "DEFAULT_GROUP_SIZE",
     "AdaptableLinear", "Linear", "Lokr", "Lora", "QuantizedLinear", "TokenEmbedding", "dequantize",
     "dequantize_rows", "layernorm_modulate", "quantize", "quantized_matmul", "workspace_size", "embedding", "lin",
-    "packed_bits", "quantize_map", "reconstruct_lokr_delta", "reconstruct_lokr_delta_scaled",
+    "packed_bits", "PackedShapeError", "quantize_map", "reconstruct_lokr_delta", "reconstruct_lokr_delta_scaled",
     "reconstruct_loha_delta",
 ]

@@ -41,6 +41,7 @@ EXPORTS = (
     "ql_quantized_matmul",
     "ql_matmul_workspace_size",
     "ql_quantized_matmul_noalloc",
+    "ql_debug_inject",
 )
 
 
@@ -94,6 +95,8 @@ def lib():
         L.ql_version.restype = i32
         L.ql_last_error.restype = C.c_char_p
         L.ql_device_error.argtypes = [i32]
+        L.ql_debug_inject.argtypes = [C.c_uint, C.c_ulonglong]
+        L.ql_debug_inject.restype = i32
         L.ql_device_error.restype = i32
         L.ql_quantize.argtypes = [vp, i32, i64, i64, i32, i32, vp, vp, vp, i32, vp]
         L.ql_dequantize.argtypes = [vp, vp, vp, i32, i64, i64, i32, i32, vp, i32, vp]
@@ -115,6 +118,17 @@ def check(status: int) -> None:
     if status != QL_OK:
         msg = lib().ql_last_error().decode(errors="replace")
         raise QlError(status, msg)
+
+
+DEV_ERR_TIMEOUT_FULL, DEV_ERR_TIMEOUT_EMPTY, DEV_ERR_TIMEOUT_ACC, DEV_ERR_BAD_INDEX = 1, 2, 4, 8
+INJECT_GEMM_PRODUCER_SILENT = 1
+
+
+def debug_inject(flags: int = 0, wait_limit_ns: int = 0) -> None:
+    """Test hook (ql_debug_inject): shortens every kernel's bounded wait to `wait_limit_ns`
+    (0 = the 2 s default) and sets injection flags (INJECT_GEMM_PRODUCER_SILENT: the tcgen05
+    GEMM's TMA producer issues nothing, so its consumers' waits run out)."""
+    check(lib().ql_debug_inject(int(flags), int(wait_limit_ns)))
 
 
 def device_error(clear: bool = True) -> int:

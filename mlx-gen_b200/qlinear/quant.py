@@ -16,10 +16,33 @@ from . import ops
 from .nn import DEFAULT_GROUP_SIZE, AdaptableLinear, TokenEmbedding
 
 
+class PackedShapeError(ValueError):
+    """A packed triple whose shapes do not describe a Q4 or Q8 affine-quantized matrix."""
+
+
 def packed_bits(wq: torch.Tensor, scales: torch.Tensor, group_size: int) -> int:
-    """``bits = wq.cols * 32 / (scales.cols * group_size)``."""
+    """``bits = wq.cols * 32 / (scales.cols * group_size)``, as src/quant.rs:38-41 infers it,
+    but with the shapes checked first: the reference indexes ``shape()[1]`` unchecked and
+    divides by a possibly zero ``in_dim``, so a 1-D or zero-width ``scales`` panics there
+    (and a non-integral or unsupported width would silently pick a wrong bit count).  Here
+    every malformed triple raises ``PackedShapeError``."""
+    if group_size not in (32, 64, 128):
+        raise PackedShapeError(f"group_size must be 32, 64 or 128 (got {group_size})")
+    if wq.dim() != 2 or scales.dim() != 2:
+        raise PackedShapeError(f"packed weight and scales must be 2-D (got {tuple(wq.shape)} and "
+                               f"{tuple(scales.shape)})")
+    if wq.shape[0] != scales.shape[0]:
+        raise PackedShapeError(f"packed weight has {wq.shape[0]} rows, scales {scales.shape[0]}")
     in_dim = scales.shape[1] * group_size
-    return wq.shape[1] * 32 // in_dim
+    if in_dim == 0 or wq.shape[1] == 0:
+        raise PackedShapeError(f"zero-width packed weight or scales ({tuple(wq.shape)}, {tuple(scales.shape)})")
+    if (wq.shape[1] * 32) % in_dim:
+        raise PackedShapeError(f"{wq.shape[1]} packed words per row do not hold a whole number of bits per "
+                               f"code over {in_dim} inputs")
+    bits = wq.shape[1] * 32 // in_dim
+    if bits not in (4, 8):
+        raise PackedShapeError(f"inferred {bits} bits per code; only 4 and 8 are supported")
+    return bits
 
 
 def _require(w: Dict[str, torch.Tensor], key: str) -> torch.Tensor:

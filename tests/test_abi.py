@@ -142,3 +142,26 @@ def test_packed_bits_and_lin_dense():
     assert q.is_quantized() and q.quantized_params()[5] == 4 and q.base_shape() == [8, 128]
     with pytest.raises(ValueError):
         q.merge_dense_delta(torch.zeros(8, 128))
+
+
+@pytest.mark.parametrize("wq_shape,s_shape,gs", [
+    ((8, 32), (8,), 64),         # 1-D scales (the reference indexes shape()[1] unchecked)
+    ((8, 32), (8, 0), 64),       # zero-width scales (the reference divides by zero)
+    ((8, 0), (8, 4), 64),        # zero-width codes
+    ((8, 12), (8, 4), 64),       # 6 bits per code
+    ((8, 16), (8, 4), 64),       # 2 bits per code
+    ((8, 33), (8, 4), 64),       # not a whole number of bits
+    ((4, 32), (8, 4), 64),       # row counts differ
+    ((8, 32), (8, 4), 48),       # unsupported group size
+    ((8,), (8, 4), 64),          # 1-D codes
+])
+def test_packed_bits_rejects_malformed_shapes(wq_shape, s_shape, gs):
+    """Malformed packed triples raise a typed error instead of the reference's panic / a
+    wrong bit count (CODE_REVIEW finding F-011 against src/quant.rs:38-41)."""
+    import torch
+    from qlinear import PackedShapeError, packed_bits
+
+    with pytest.raises(PackedShapeError):
+        packed_bits(torch.zeros(wq_shape, dtype=torch.int32), torch.zeros(s_shape, dtype=torch.bfloat16), gs)
+    with pytest.raises(ValueError):  # it is a ValueError too
+        packed_bits(torch.zeros(wq_shape, dtype=torch.int32), torch.zeros(s_shape, dtype=torch.bfloat16), gs)
