@@ -145,7 +145,7 @@ def run_reference(args):
     import oracle as O  # CPU restatement of MLX's affine quantized_matmul
 
     cfg = dict(FLUX)
-    Ms = 32  # bounded sample: 32 of the 4608 tokens per step
+    Ms = 256  # bounded sample: 256 of the 4608 tokens per step
     rng = np.random.default_rng(0)
     lin = []
     for name, N, K, act, _, _ in flux_linears(cfg):
@@ -175,7 +175,8 @@ def run_reference(args):
            "config": {"workload": "flux_q8_block_linears", "M": cfg["M"], "sample_tokens": Ms, "bits": 8,
                       "group_size": 64},
            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                            "sample": f"{Ms} of {cfg['M']} tokens through the 4 FLUX block linears per step"},
+                            "sample": f"{Ms} of {cfg['M']} tokens through the 4 FLUX block linears per step",
+                            "host_cpu": host_cpu()},
            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
            "note": "MLX (the reference's backend) cannot be built here; this is the CPU oracle "
                    "restatement (oracle/qref.c) pinned to the reference fixture"}
@@ -184,27 +185,108 @@ def run_reference(args):
 
 # ----------------------------------------------------------------------------- GPU arm
 
-def cpu_baseline_sample(cfg):
+def host_cpu():
+    """Model name and logical CPU count of the host (from /proc/cpuinfo)."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"model": model, "logical_cpus": os.cpu_count()}
+
+
+def cpu_baseline_sample(cfg, tokens=(256, 32)):
+    """The oracle's fast mode (pthreads, all host threads) on the first `tokens[0]` tokens of
+    the FLUX block's four linears; the rate at the other sample sizes shows how flat the CPU
+    rate is in M."""
     import numpy as np
 
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
 
-    Ms = 32
     rng = np.random.default_rng(1)
     threads = os.cpu_count() or 1
-    t_total, flops = 0.0, 0.0
+    lin = []
     for name, N, K, act, _, _ in flux_linears(cfg):
         w = O.to_bf16((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
-        wq, s, b = O.quantize(w, cfg["gs"], cfg["bits"])
-        x = O.to_bf16(rng.standard_normal((Ms, K)).astype(np.float32))
-        O.quantized_matmul_fast(x, wq, s, b, cfg["gs"], cfg["bits"], threads=threads)  # warm
-        t0 = time.perf_counter()
-        O.quantized_matmul_fast(x, wq, s, b, cfg["gs"], cfg["bits"], threads=threads)
-        t_total += time.perf_counter() - t0
-        flops += 2.0 * Ms * N * K
-    return {"value": flops / t_total / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{Ms} of {cfg['M']} tokens through the 4 FLUX block linears (oracle fast mode)"}
+        lin.append((N, K) + O.quantize(w, cfg["gs"], cfg["bits"]))
+    rates = {}
+    for Ms in tokens:
+        t_total, flops = 0.0, 0.0
+        for N, K, wq, s, b in lin:
+            x = O.to_bf16(rng.standard_normal((Ms, K)).astype(np.float32))
+            O.quantized_matmul_fast(x, wq, s, b, cfg["gs"], cfg["bits"], threads=threads)  # warm
+            t0 = time.perf_counter()
+            O.quantized_matmul_fast(x, wq, s, b, cfg["gs"], cfg["bits"], threads=threads)
+            t_total += time.perf_counter() - t0
+            flops += 2.0 * Ms * N * K
+        rates[Ms] = flops / t_total / 1e12
+    Ms = tokens[0]
+    return {"value": rates[Ms], "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{Ms} of {cfg['M']} tokens through the 4 FLUX block linears (oracle fast mode)",
+            "rate_by_tokens": {str(k): v for k, v in rates.items()}, "host_cpu": host_cpu()}
+
+
+def timed_flushed(fn, iters, flush):
+    """Mean CUDA-event time (ms) of fn over `iters` calls, with an L2 flush (a write larger
+    than the 126 MB L2) before each call, outside the timed events."""
+    import torch
+
+    fn()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(iters):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        tot += e0.elapsed_time(e1)
+    return tot / iters
+
+
+def quant_dequant(dev, peaks, iters=10):
+    """quantize (bf16 W -> packed Q4 g64) and dequantize (-> bf16) in HBM GB/s, algorithmic
+    bytes: quantize N*K*2 + N*K*bits/8 + N*(K/gs)*4, dequantize N*K*bits/8 + N*(K/gs)*4 +
+    N*K*2.  W of cfg1 (3072 x 3072) and of the Wan FFN up projection (13824 x 5120); L2
+    flushed before every call."""
+    import torch
+    import qlinear
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(21)
+    out = {}
+    for name, N, K, bits, gs in (("cfg1_w_q4", 3072, 3072, 4, 64), ("wan_ffn_w_q4", 13824, 5120, 4, 64)):
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        wq, s, b = qlinear.quantize(w, gs, bits)
+        deq = torch.empty(N, K, dtype=torch.bfloat16, device=dev)
+        qb = N * K * 2 + N * K * bits // 8 + N * (K // gs) * 4
+        db = N * K * bits // 8 + N * (K // gs) * 4 + N * K * 2
+        from qlinear import _lib, ops
+        import ctypes as C
+
+        def q():
+            _lib.check(_lib.lib().ql_quantize(ops._ptr(w), _lib.QL_BF16, N, K, gs, bits, ops._ptr(wq), ops._ptr(s),
+                                              ops._ptr(b), _lib.QL_BF16, ops._stream(dev)))
+
+        def d():
+            _lib.check(_lib.lib().ql_dequantize(ops._ptr(wq), ops._ptr(s), ops._ptr(b), _lib.QL_BF16, N, K, gs, bits,
+                                                ops._ptr(deq), _lib.QL_BF16, ops._stream(dev)))
+
+        qms, dms = timed_flushed(q, iters, flush), timed_flushed(d, iters, flush)
+        out[name] = {"shape": f"{N}x{K} Q{bits} g{gs}",
+                     "quantize": {"value": qb / (qms * 1e-3) / 1e9, "unit": "GB/s", "us": qms * 1e3, "bytes": qb,
+                                  "frac_of_hbm": qb / (qms * 1e-3) / 1e9 / peaks["hbm_gbs"]},
+                     "dequantize": {"value": db / (dms * 1e-3) / 1e9, "unit": "GB/s", "us": dms * 1e3, "bytes": db,
+                                    "frac_of_hbm": db / (dms * 1e-3) / 1e9 / peaks["hbm_gbs"]}}
+        del w, wq, s, b, deq
+    assert qlinear.device_error() == 0
+    return out
 
 
 def decode_gemv(dev, steps=20, warmup=5, M=1, head=True):
@@ -684,6 +766,7 @@ def run_ours(args):
                 result["decode_gemv"][f"M{m}"] = {"value": d["value"], "unit": "GB/s", "ms_per_step": d["ms_per_step"],
                                                   "frac_of_hbm": d["value"] / peaks["hbm_gbs"]}
             result["other_configs"] = other_configs(dev)
+            result["quant_dequant"] = quant_dequant(dev, peaks)
         print(json.dumps(result), file=json_out, flush=True)
     if comm is not None:
         comm.close()

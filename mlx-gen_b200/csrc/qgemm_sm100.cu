@@ -535,7 +535,13 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                         for (int t = 0; t < 4; ++t) r[4 * i + t] = hfma2_bf16(qp[t], ss, bb);
                     }
                 } else {
-                    const float fs0 = bf16lo(s0), fb0 = bf16lo(b0), fs1 = bf16lo(s1), fb1 = bf16lo(b1);
+                    // A code byte c placed in bits 8-15 of 0x47000000 reads as the float
+                    // 32768 + c (one prmt).  s * (32768 + c) is exact in fp32 (8 x 16
+                    // significant bits), so fma(s, 32768 + c, b - 32768 s) is the fp32
+                    // rounding of s c + b whenever b - 32768 s is exact -- the same value
+                    // as fma(c, s, b) -- and within an fp32 ulp of 32768 s otherwise.
+                    const float fs0 = bf16lo(s0), fs1 = bf16lo(s1);
+                    const float fb0 = fmaf(-32768.f, fs0, bf16lo(b0)), fb1 = fmaf(-32768.f, fs1, bf16lo(b1));
 #pragma unroll
                     for (int h = 0; h < 4; ++h) {
                         uint4 a = wrow[h ^ ((row >> 1) & 3)];
@@ -544,10 +550,10 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                         for (int i = 0; i < 4; ++i) {
                             const int wi = 4 * h + i;  // word index: codes 4wi..4wi+3
                             const float ss = wi < 8 ? fs0 : fs1, bb = wi < 8 ? fb0 : fb1;
-                            const float c0 = fmaf(q8_code_f32(wv[i], 0), ss, bb);
-                            const float c1 = fmaf(q8_code_f32(wv[i], 1), ss, bb);
-                            const float c2 = fmaf(q8_code_f32(wv[i], 2), ss, bb);
-                            const float c3 = fmaf(q8_code_f32(wv[i], 3), ss, bb);
+                            const float c0 = fmaf(__uint_as_float(prmt(wv[i], 0x47000000u, 0x7604u)), ss, bb);
+                            const float c1 = fmaf(__uint_as_float(prmt(wv[i], 0x47000000u, 0x7614u)), ss, bb);
+                            const float c2 = fmaf(__uint_as_float(prmt(wv[i], 0x47000000u, 0x7624u)), ss, bb);
+                            const float c3 = fmaf(__uint_as_float(prmt(wv[i], 0x47000000u, 0x7634u)), ss, bb);
                             r[2 * wi] = pack_bf16x2(c0, c1);
                             r[2 * wi + 1] = pack_bf16x2(c2, c3);
                         }
