@@ -297,7 +297,7 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                 bp = p.bias;
             }
             const bool has_bias = bp != nullptr;
-            const float bias = (has_bias && n < p.N) ? __bfloat162float(bp[n]) : 0.f;
+            const uint32_t bias2 = (has_bias && n < p.N) ? 0x10001u * reinterpret_cast<const uint16_t *>(bp)[n] : 0u;
             if (!mbar_wait<CG == 2>(accfull, tcount & 1, abort_flag, DEV_ERR_TIMEOUT_ACC, peer_abort)) break;
             tc_fence_after();
 #pragma unroll 1
@@ -307,13 +307,8 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    float a = round_bf16(__uint_as_float(v[2 * i]));
-                    float b = round_bf16(__uint_as_float(v[2 * i + 1]));
-                    if (has_bias) {
-                        a += bias;
-                        b += bias;
-                    }
-                    pk[i] = pack_bf16x2(a, b);
+                    pk[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+                    if (has_bias) pk[i] = hfma2_bf16(pk[i], 0x3f803f80u, bias2);
                 }
                 tmem_st16(lane_base + STG_COL + c * 16, pk);
             }
