@@ -1,15 +1,17 @@
 // quantize.cu -- group-wise affine quantize / dequantize kernels.
 //
-// Both kernels are HBM-bound streaming kernels: one thread per packed uint32
-// word (8 Q4 codes or 4 Q8 codes), so a warp reads/writes contiguous 128-byte
-// segments.  A group of `gs` elements is covered by gs*bits/32 consecutive
-// lanes; the group's min/max is a shuffle-xor reduction among them.
+// Both kernels are HBM-bound streaming kernels.  quantize: one thread per packed
+// uint32 word (8 Q4 codes or 4 Q8 codes), so a warp reads/writes contiguous 128-byte
+// segments; a group of `gs` elements is covered by gs*bits/32 consecutive lanes and
+// its min/max is a shuffle-xor reduction among them.  dequantize: one thread per
+// 16 bytes of packed codes (one group's scale and bias), 16-byte stores.
 //
 // Arithmetic follows MLX affine quantization as the reference calls it
 // (src/quant.rs:140, src/adapters.rs:533-537; restated and pinned against the
 // reference fixture in oracle/qref.c quant_group()).  Every division is an
-// IEEE round-to-nearest division and no multiply-add is contracted, so the
-// codes, scales and biases are bit-identical to the oracle.
+// IEEE round-to-nearest division (or provably equal to one, see the code loop) and
+// no multiply-add is contracted, so the codes, scales and biases are bit-identical
+// to the oracle.
 #include "ql_common.cuh"
 
 namespace ql {
@@ -61,27 +63,33 @@ __global__ void __launch_bounds__(256) quantize_kernel(const void *__restrict__ 
                                                        uint32_t *__restrict__ wq,
                                                        void *__restrict__ scales,
                                                        void *__restrict__ biases, int sb_dtype) {
+    // Each thread packs 2 consecutive words (16 / 8 elements); a group spans
+    // tpg = gs / (2 * EPW) consecutive lanes (a power of two in [2, 16]).
     constexpr int EPW = 32 / BITS;
-    const int tpg = gs / EPW;  // lanes per group: power of two in [4, 32]
+    const int tpg = gs / (2 * EPW);
     const float n_bins = (float)((1 << BITS) - 1);
+    const int64_t pairs = total_words / 2;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    // total_words is a multiple of tpg, and tpg divides 32, so every lane of a
-    // group runs the same number of iterations (the shuffles stay converged).
-    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-         t - (threadIdx.x & 31) < total_words; t += stride) {
-        const bool live = t < total_words;
-        float v[EPW];
-        if (live) load_elems<EPW>(w, w_dtype, t * EPW, v);
-        else {
+    // pairs is a multiple of tpg, and tpg divides 32, so every lane of a group runs
+    // the same number of iterations (the shuffles stay converged).
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t - (threadIdx.x & 31) < pairs; t += stride) {
+        const bool live = t < pairs;
+        float v[2][EPW];
+        if (live) {
+            load_elems<EPW>(w, w_dtype, 2 * t * EPW, v[0]);
+            load_elems<EPW>(w, w_dtype, (2 * t + 1) * EPW, v[1]);
+        } else {
 #pragma unroll
-            for (int i = 0; i < EPW; ++i) v[i] = 0.f;
+            for (int i = 0; i < EPW; ++i) v[0][i] = v[1][i] = 0.f;
         }
-        float mn = v[0], mx = v[0];
+        float mn = v[0][0], mx = v[0][0];
 #pragma unroll
-        for (int i = 1; i < EPW; ++i) {
-            mn = fminf(mn, v[i]);
-            mx = fmaxf(mx, v[i]);
-        }
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int i = 0; i < EPW; ++i) {
+                mn = fminf(mn, v[h][i]);
+                mx = fmaxf(mx, v[h][i]);
+            }
         for (int o = 1; o < tpg; o <<= 1) {
             mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -97,14 +105,28 @@ __global__ void __launch_bounds__(256) quantize_kernel(const void *__restrict__ 
             s = __fdiv_rn(edge, q0);
             b = edge;
         }
-        uint32_t word = 0;
+        // code = clamp(rint((v - b) / s)) with the IEEE quotient.  The quotient is first
+        // taken as a product with the rounded reciprocal, within 2 ulps (relative 2^-22) of
+        // the exact one: below -1 or above 300 the clamp decides the code either way, and
+        // inside [-1, 300] the product is within 2^-13 of the quotient, so rint agrees
+        // unless the product lies within 2^-10 of a rounding boundary (x.5); only then (or
+        // for a NaN) is the exact division done.  The codes are the exact ones.
+        const float rs = __frcp_rn(s);
+        uint32_t word[2] = {0u, 0u};
 #pragma unroll
-        for (int i = 0; i < EPW; ++i) {
-            float c = rintf(__fdiv_rn(__fsub_rn(v[i], b), s));
-            c = fminf(fmaxf(c, 0.0f), n_bins);
-            word |= (uint32_t)c << (BITS * i);
-        }
-        wq[t] = word;
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int i = 0; i < EPW; ++i) {
+                const float a = __fsub_rn(v[h][i], b);
+                float qf = __fmul_rn(a, rs);
+                const float fr = qf - floorf(qf);
+                const bool in_range = qf >= -1.0f && qf <= 300.0f;
+                if ((in_range && fabsf(fr - 0.5f) < 0x1p-10f) || qf != qf) qf = __fdiv_rn(a, s);
+                float c = rintf(qf);
+                c = fminf(fmaxf(c, 0.0f), n_bins);
+                word[h] |= (uint32_t)c << (BITS * i);
+            }
+        reinterpret_cast<uint2 *>(wq)[t] = make_uint2(word[0], word[1]);
         if ((t % tpg) == 0) {
             const int64_t g = t / tpg;
             store_from_f32(scales, sb_dtype, g, s);
@@ -113,7 +135,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(const void *__restrict__ 
     }
 }
 
-// One thread per packed word of the output rows.  ids == nullptr: row r reads
+// ids == nullptr: row r reads
 // packed row r; otherwise packed row ids[r] (quantized embedding gather).  round_sb: the
 // value is first rounded to the scales' dtype (mlx's dequantize output) and then converted
 // to out_dtype, as the reference's gather + dequantize + cast does.
@@ -122,58 +144,62 @@ __global__ void __launch_bounds__(256) dequantize_kernel(
     const int64_t *__restrict__ ids, int64_t rows, int64_t N, int64_t words_per_row, int gs,
     const uint32_t *__restrict__ wq, const void *__restrict__ scales,
     const void *__restrict__ biases, int sb_dtype, void *__restrict__ out, int out_dtype, bool round_sb) {
+    // Each thread handles 4 consecutive packed words (16 bytes: 32 Q4 / 16 Q8 codes, always
+    // inside one group since a row holds a multiple of 32 codes and gs >= 32).
     constexpr int EPW = 32 / BITS;
-    const int64_t total = rows * words_per_row;
+    constexpr int E4 = 4 * EPW;
+    const int64_t qpr = words_per_row / 4;  // 16-byte quads per row
+    const int64_t total = rows * qpr;
     const int64_t G = words_per_row * EPW / gs;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
-        const int64_t r = t / words_per_row, wi = t - r * words_per_row;
+        const int64_t r = t / qpr, qi = t - r * qpr;
         int64_t n = r;
         bool ok = true;
         if (ids) {
             n = __ldg(ids + r);
             if (n < 0 || n >= N) {
                 ok = false;
-                if (wi == 0) raise_dev_error(DEV_ERR_BAD_INDEX);
+                if (qi == 0) raise_dev_error(DEV_ERR_BAD_INDEX);
             }
         }
-        float o[EPW];
+        uint32_t words[4] = {0u, 0u, 0u, 0u};
+        float s = 0.f, b = 0.f;
         if (ok) {
-            const uint32_t word = __ldg(wq + n * words_per_row + wi);
-            const int64_t g = n * G + (wi * EPW) / gs;
-            const float s = load_as_f32(scales, sb_dtype, g);
-            const float b = load_as_f32(biases, sb_dtype, g);
-#pragma unroll
-            for (int i = 0; i < EPW; ++i) {
-                o[i] = fmaf((float)((word >> (BITS * i)) & ((1u << BITS) - 1u)), s, b);
-                if (round_sb) o[i] = round_to(sb_dtype, o[i]);
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < EPW; ++i) o[i] = 0.f;
+            const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(wq + n * words_per_row) + qi);
+            words[0] = wv.x, words[1] = wv.y, words[2] = wv.z, words[3] = wv.w;
+            const int64_t g = n * G + (qi * E4) / gs;
+            s = load_as_f32(scales, sb_dtype, g);
+            b = load_as_f32(biases, sb_dtype, g);
         }
-        const int64_t e = t * EPW;  // == r*K + wi*EPW
+        // element k of the quad: code (words[k / EPW] >> (BITS * (k % EPW))) & mask
+        auto val = [&](int k) -> float {
+            if (!ok) return 0.f;
+            float v = fmaf((float)((words[k / EPW] >> (BITS * (k % EPW))) & ((1u << BITS) - 1u)), s, b);
+            return round_sb ? round_to(sb_dtype, v) : v;
+        };
+        const int64_t e = t * E4;  // == r*K + qi*E4
         if (out_dtype == QL_F32) {
             float4 *p = reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + e);
 #pragma unroll
-            for (int i = 0; i < EPW / 4; ++i)
-                p[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            for (int i = 0; i < E4 / 4; ++i) p[i] = make_float4(val(4 * i), val(4 * i + 1), val(4 * i + 2), val(4 * i + 3));
         } else {
-            uint32_t packed[EPW / 2];
+            uint4 *p = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(out) + e);
 #pragma unroll
-            for (int i = 0; i < EPW / 2; ++i) {
-                if (out_dtype == QL_BF16) {
-                    packed[i] = pack_bf16x2(o[2 * i], o[2 * i + 1]);
-                } else {
-                    __half2 h = __floats2half2_rn(o[2 * i], o[2 * i + 1]);
-                    packed[i] = *reinterpret_cast<uint32_t *>(&h);
+            for (int i = 0; i < E4 / 8; ++i) {
+                uint32_t pk[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float lo = val(8 * i + 2 * j), hi = val(8 * i + 2 * j + 1);
+                    if (out_dtype == QL_BF16) {
+                        pk[j] = pack_bf16x2(lo, hi);
+                    } else {
+                        __half2 h = __floats2half2_rn(lo, hi);
+                        pk[j] = *reinterpret_cast<uint32_t *>(&h);
+                    }
                 }
+                p[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
-            uint16_t *p = reinterpret_cast<uint16_t *>(out) + e;
-            if constexpr (EPW == 8)
-                *reinterpret_cast<uint4 *>(p) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            else
-                *reinterpret_cast<uint2 *>(p) = make_uint2(packed[0], packed[1]);
         }
     }
 }
@@ -190,8 +216,8 @@ static int grid_for(int64_t work, int block) {
 
 int launch_quantize(const void *w, int w_dtype, int64_t N, int64_t K, int gs, int bits,
                     uint32_t *wq, void *scales, void *biases, int sb_dtype, cudaStream_t st) {
-    const int64_t words = N * K * bits / 32;
-    const int grid = grid_for(words, 256);
+    const int64_t words = N * K * bits / 32;  // even: K is a multiple of 32
+    const int grid = grid_for(words / 2, 256);
     if (bits == 4)
         quantize_kernel<4><<<grid, 256, 0, st>>>(w, w_dtype, words, gs, wq, scales, biases, sb_dtype);
     else
@@ -204,7 +230,7 @@ int launch_dequantize(const int64_t *ids, int64_t rows, int64_t N, int64_t K, in
                       const uint32_t *wq, const void *scales, const void *biases, int sb_dtype,
                       void *out, int out_dtype, bool round_sb, cudaStream_t st) {
     const int64_t wpr = K * bits / 32;
-    const int grid = grid_for(rows * wpr, 256);
+    const int grid = grid_for(rows * wpr / 4, 256);
     if (bits == 4)
         dequantize_kernel<4><<<grid, 256, 0, st>>>(ids, rows, N, wpr, gs, wq, scales, biases,
                                                     sb_dtype, out, out_dtype, round_sb);
