@@ -170,6 +170,16 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
  * epilogue (0 when none; the LoRA residual needs M * round_up(rank, 64) * 2). */
 size_t ql_matmul_workspace_size(int64_t M, int64_t N, int64_t K, const ql_epilogue *ep);
 
+/* Workspace for ql_quantized_matmul when x is x_dtype: the LoRA need above, or -- for f32 /
+ * f16 activations -- the two bf16 pieces of x ([M, 2 * round_up(K, 64)] bf16) that the
+ * tensor-core path for those dtypes stages.  Given that workspace, an f32 / f16 x with bf16
+ * or f16 scales, f32 / f16 y, a plain or GELU linear (no SwiGLU, LoRA, LoKr or gated
+ * residual) runs on the tcgen05 GEMM in three bf16 passes (x and each dequantized weight
+ * split into two bf16 pieces: about 16 significant bits per product, fp32 accumulation --
+ * the activations of FLUX.2 / Qwen image streams / LTX text encoders, src/adapters.rs:252,
+ * src/nn.rs:295); without it those calls run on the CUDA-core kernel. */
+size_t ql_matmul_workspace_size_x(int64_t M, int64_t N, int64_t K, const ql_epilogue *ep, int x_dtype);
+
 /* Same as ql_quantized_matmul, for callers that cannot allocate device memory
  * (allocator hooks, real-time loops that must not enter the driver's allocator,
  * runtimes whose memory is fully reserved).  No counterpart in the reference.

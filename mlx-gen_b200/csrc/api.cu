@@ -48,6 +48,9 @@ int launch_qmm_generic(const void *, int, int64_t, int64_t, const uint32_t *, co
                        const void *, const uint32_t *, const void *, const void *, int, int64_t, int,
                        int, const void *, const void *, int, const void *, const void *, int64_t,
                        float, void *, int, const Gated &, const void *, float, cudaStream_t);
+size_t qgemm_x3_workspace(int64_t M, int64_t K);
+int launch_qgemm_x3(const void *, int, int64_t, int64_t, const uint32_t *, const void *, const void *, int, int64_t,
+                    int, int, const void *, int, void *, int, void *, int, cudaStream_t);
 int launch_lora_t(const void *, int64_t, int64_t, const void *, int64_t, float, void *, cudaStream_t);
 int launch_ln_modulate(const void *, int64_t, int64_t, float, const void *, const void *, int64_t, void *, int,
                        cudaStream_t);
@@ -156,6 +159,15 @@ int ql_dequantize_rows(const int64_t *ids, int64_t R, const uint32_t *wq, const 
                              out_dtype, true, (cudaStream_t)stream);
 }
 
+size_t ql_matmul_workspace_size_x(int64_t M, int64_t N, int64_t K, const ql_epilogue *ep, int x_dtype) {
+    size_t w = ql_matmul_workspace_size(M, N, K, ep);
+    if ((x_dtype == QL_F32 || x_dtype == QL_F16) && M > 0 && K > 0) {
+        const size_t x3 = qgemm_x3_workspace(M, K);
+        if (x3 > w) w = x3;
+    }
+    return w;
+}
+
 size_t ql_matmul_workspace_size(int64_t M, int64_t N, int64_t K, const ql_epilogue *ep) {
     (void)N;
     (void)K;
@@ -199,6 +211,21 @@ int ql_quantized_matmul(const void *x, int x_dtype, int64_t M, int64_t K, const 
     const bool lokr = e.lokr_delta != nullptr;
     if (lokr && swiglu) return fail(QL_EUNSUPPORTED, "a LoKr delta cannot be fused with SwiGLU");
     if (lokr && !aligned16(e.lokr_delta)) return fail(QL_EINVAL_ARG, "lokr_delta must be 16-byte aligned");
+    // f32 / f16 activations on the tensor cores (three-pass bf16 split) when the caller gave
+    // the workspace for the split activations (ql_matmul_workspace_size_x); the CUDA-core
+    // generic kernel otherwise
+    const bool x3_shape = (x_dtype == QL_F32 || x_dtype == QL_F16) && sb_dtype != QL_F32 &&
+                          (y_dtype == QL_F32 || y_dtype == QL_F16) && !swiglu && !lora && !gd.res && !lokr &&
+                          (e.act == QL_ACT_NONE || e.act == QL_ACT_GELU_TANH || e.act == QL_ACT_GELU_ERF);
+    if (x3_shape && ((e.kernel == QL_KERNEL_AUTO && M > 8) || e.kernel == QL_KERNEL_GEMM) && e.workspace &&
+        e.workspace_bytes >= qgemm_x3_workspace(M, K)) {
+        if (!aligned16(e.workspace)) return fail(QL_EINVAL_ARG, "workspace must be 16-byte aligned");
+        return launch_qgemm_x3(x, x_dtype, M, K, wq, scales, biases, sb_dtype, N, group_size, bits, e.bias, e.act, y,
+                               y_dtype, e.workspace, e.max_ctas, st);
+    }
+    if (e.kernel == QL_KERNEL_GEMM && !tc_dtypes)
+        return fail(QL_EUNSUPPORTED, "the tensor-core GEMM with f32 / f16 activations needs a plain or GELU linear "
+                                     "with bf16 or f16 scales and the workspace of ql_matmul_workspace_size_x");
     if (kernel == QL_KERNEL_AUTO)
         kernel = !tc_dtypes ? QL_KERNEL_GENERIC : ((M <= 8 && !lokr) ? QL_KERNEL_GEMV : QL_KERNEL_GEMM);
     if (lokr && kernel != QL_KERNEL_GEMM && kernel != QL_KERNEL_GENERIC)

@@ -113,7 +113,16 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)
 // Params block measurably slowed the plain kernel).
 // LOKR: the dequant warps add lokr_scale * dW (a dense bf16 [N, K] delta staged by TMA with
 // the packed weights) to each dequantized weight, so a LoKr adapter costs no extra MMA.
-template <int BITS, bool SWIGLU, int CG, bool GATED, bool LOKR = false>
+// X3: the split path for f32 / f16 activations.  x arrives as two bf16 pieces (x = hi +
+// lo, [M, 2 * Kp] with Kp = ktw * BK, lo at column Kp) and each dequantized weight w (fp32,
+// one rounding as the reference's dequantize) as two bf16 pieces (w = whi + wlo); the
+// k-steps run three times over K -- whi.hi, whi.lo, wlo.hi -- into the one fp32
+// accumulator, and the epilogue writes f32 or f16.  See launch_qgemm_x3.
+constexpr int QL_EPI_OUT_F32 = 0x200;  // Params::act flags of the X3 path
+constexpr int QL_EPI_OUT_F16 = 0x400;
+constexpr int QL_EPI_SB_F16 = 0x800;
+
+template <int BITS, bool SWIGLU, int CG, bool GATED, bool LOKR = false, bool X3 = false>
 __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtensorMap &tm_w, const CUtensorMap &tm_w2,
                                            const CUtensorMap &tm_t, const Params &p, const Gated &gd,
                                            const CUtensorMap *tm_d = nullptr, uint32_t lokr_scale2 = 0) {
@@ -143,7 +152,7 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
     const uint32_t rank = CG == 2 ? cluster_ctarank() : 0;
     const int cid = (int)blockIdx.x / CG, ncl = (int)gridDim.x / CG;
     const int num_tiles = p.num_w_tiles * p.num_t_tiles;
-    const int KT = p.ktw + p.ktl;
+    const int KT = X3 ? 3 * p.ktw : p.ktw + p.ktl;
     // shared::cluster addresses in the leader CTA (rank 0) / of the peer's abort flag
     auto leader = [&](const void *local) -> uint32_t {
         return CG == 2 ? mapa_shared(smem_u32(local), 0) : smem_u32(local);
@@ -189,7 +198,9 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
             for (int tile = cid; tile < num_tiles && !*abort_flag; tile += ncl) {
                 const int wt = tile % p.num_w_tiles, tt = tile / p.num_w_tiles;
                 const int xrow = tt * BT + (int)rank * C::XROWS;
-                for (int kt = 0; kt < KT; ++kt, ++it) {
+                for (int kk = 0; kk < KT; ++kk, ++it) {
+                    // X3: segment seg of the three passes over K, k-step kt inside it
+                    const int seg = X3 ? kk / p.ktw : 0, kt = X3 ? kk - seg * p.ktw : kk;
                     const int s = it % STAGES;
                     if (!mbar_wait<CG == 2>(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY,
                                    peer_abort))
@@ -202,11 +213,11 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                     }
                     uint8_t *xs = smem + C::SMEM_X + s * C::X_STAGE_BYTES;
                     uint8_t *ws = smem + C::SMEM_W + s * C::W_STAGE_BYTES;
-                    const bool wstep = kt < p.ktw;
+                    const bool wstep = X3 || kt < p.ktw;
                     // x half (or LoRA T half): counted on the leader's xfull[s]
                     if (rank == 0) mbar_arrive_expect_tx(&xfull[s], CG * C::X_STAGE_BYTES);
                     const CUtensorMap *xm = wstep ? &tm_x : &tm_t;
-                    const int xk = wstep ? kt * BK : (kt - p.ktw) * BK;
+                    const int xk = X3 ? (seg == 1 ? p.ktw * BK : 0) + kt * BK : (wstep ? kt * BK : (kt - p.ktw) * BK);
                     if (CG == 2) tma_load_2d_pair(xs, xm, leader(&xfull[s]), xk, xrow);
                     else tma_load_2d(xs, xm, &xfull[s], xk, xrow);
                     // packed W rows of this CTA: counted on the local wfull[s]
@@ -300,6 +311,42 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
             const uint32_t bias2 = (has_bias && n < p.N) ? 0x10001u * reinterpret_cast<const uint16_t *>(bp)[n] : 0u;
             if (!mbar_wait<CG == 2>(accfull, tcount & 1, abort_flag, DEV_ERR_TIMEOUT_ACC, peer_abort)) break;
             tc_fence_after();
+            if constexpr (X3) {
+                // f32 / f16 output straight from the accumulator (long-K tiles: the drain is a
+                // small part of the tile); the reference's rounding points in the output dtype
+                const bool f32o = (p.act & QL_EPI_OUT_F32) != 0;
+                const int act = p.act & 0xff;
+                float bias_f = 0.f;
+                if (has_bias && n < p.N)
+                    bias_f = f32o ? reinterpret_cast<const float *>(bp)[n]
+                                  : __half2float(reinterpret_cast<const __half *>(bp)[n]);
+                const int m0 = tt * BT;
+#pragma unroll 1
+                for (int c = 0; c < BT / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld32(lane_base + ACC_COL + c * 32, v);
+                    tmem_ld_wait();
+                    if (n < p.N) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const int m = m0 + c * 32 + i;
+                            float a = __uint_as_float(v[i]);
+                            if (!f32o) a = __half2float(__float2half_rn(a));
+                            if (has_bias) a = f32o ? a + bias_f : __half2float(__float2half_rn(a + bias_f));
+                            if (act == QL_ACT_GELU_TANH) a = 0.5f * a * (1.0f + tanhf(0.7978845608028654f * (a + 0.044715f * a * a * a)));
+                            else if (act == QL_ACT_GELU_ERF) a = gelu_erf_f(a);
+                            if (m < p.M) {
+                                if (f32o) reinterpret_cast<float *>(p.y)[(int64_t)m * p.N + n] = a;
+                                else reinterpret_cast<__half *>(p.y)[(int64_t)m * p.N + n] = __float2half_rn(a);
+                            }
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(accempty);
+                continue;
+            }
 #pragma unroll 1
             for (int c = 0; c < BT / 32; ++c) {
                 uint32_t v[32], pk[16];
@@ -438,14 +485,17 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
         uint32_t it = 0;
         bool ok = true;
         if (nchunk > 0) load_chunk(0, 0, nxt);
+        constexpr int NSEG = X3 ? 3 : 1;  // X3: the scales of every pass over K
         for (int lt = 0; lt < my_tiles && ok; ++lt) {
-            for (int c = 0; c < nchunk && ok; ++c) {
+            for (int cs = 0; cs < NSEG * nchunk && ok; ++cs) {
+                const int c = cs % nchunk;
 #pragma unroll
                 for (int r4 = 0; r4 < 4; ++r4)
 #pragma unroll
                     for (int i = 0; i < 8; ++i) cur[r4][i] = nxt[r4][i];
-                // prefetch the next chunk (of this tile, or the first of the next tile)
+                // prefetch the next chunk (of this tile and pass, the next pass, or the next tile)
                 if (c + 1 < nchunk) load_chunk(lt, c + 1, nxt);
+                else if (cs + 1 < NSEG * nchunk) load_chunk(lt, 0, nxt);
                 else load_chunk(lt + 1, 0, nxt);
                 // k-steps whose first group lies in chunk c
                 const int kt0 = (c * 8 * p.gs + BK - 1) / BK;
@@ -469,7 +519,7 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                 }
             }
             // LoRA k-steps of this tile: no scales (the dequant warps do not read the slot)
-            for (int kt = p.ktw; kt < KT && ok; ++kt, ++it) {
+            for (int kt = p.ktw; kt < (X3 ? p.ktw : KT) && ok; ++kt, ++it) {
                 const int slot = it % SBR;
                 if (!mbar_wait<false>(&sbempty[slot], ((it / SBR) & 1) ^ 1, abort_flag, DEV_ERR_TIMEOUT_EMPTY)) {
                     ok = false;
@@ -508,7 +558,42 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                                                                  DEV_ERR_TIMEOUT_EMPTY, peer_abort)))
                 break;
             uint32_t r[32];
-            if (kt < p.ktw) {
+            if constexpr (X3) {
+                // w = fma(code, s, b) in fp32 (the reference's dequantize), then the bf16 piece
+                // of this pass: whi = bf16(w) for passes 0 and 1, wlo = bf16(w - whi) for pass 2
+                const bool lo_pass = kt >= 2 * p.ktw;
+                const bool sb16 = (p.act & QL_EPI_SB_F16) != 0;
+                auto sbf = [&](uint32_t v) { return sb16 ? __half2float(__ushort_as_half((unsigned short)v)) : bf16lo(v); };
+                const float fs0 = sbf(sb[0]), fb0 = sbf(sb[1]), fs1 = sbf(sb[2]), fb1 = sbf(sb[3]);
+                const uint4 *wrow = reinterpret_cast<const uint4 *>(smem + C::SMEM_W + s * C::W_STAGE_BYTES +
+                                                                    row * C::W_ROW_BYTES);
+                uint32_t wv[BITS * 2];  // the step's 64 codes: 8 (Q4) / 16 (Q8) words
+                if constexpr (BITS == 4) {
+                    const int sw = (row >> 2) & 1;
+                    const uint4 a = wrow[sw], b = wrow[sw ^ 1];
+                    wv[0] = a.x, wv[1] = a.y, wv[2] = a.z, wv[3] = a.w, wv[4] = b.x, wv[5] = b.y, wv[6] = b.z, wv[7] = b.w;
+                } else {
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        const uint4 a = wrow[h ^ ((row >> 1) & 3)];
+                        wv[4 * h] = a.x, wv[4 * h + 1] = a.y, wv[4 * h + 2] = a.z, wv[4 * h + 3] = a.w;
+                    }
+                }
+                // an f16 computation dtype (f16 x and scales) rounds w to f16 first, as the
+                // reference's f16 quantized_matmul does; f16 has 11 bits, so whi + wlo hold it exactly
+                const bool w16 = (p.act & QL_EPI_OUT_F16) != 0;
+                auto piece = [&](int k) -> float {
+                    constexpr int EPW = 32 / BITS;
+                    const uint32_t code = (wv[k / EPW] >> (BITS * (k % EPW))) & ((1u << BITS) - 1u);
+                    float w = fmaf(__uint_as_float(0x4B000000u | code) - 8388608.0f, k < 32 ? fs0 : fs1,
+                                   k < 32 ? fb0 : fb1);
+                    if (w16) w = __half2float(__float2half_rn(w));
+                    const float hi = round_bf16(w);
+                    return lo_pass ? w - hi : hi;
+                };
+#pragma unroll
+                for (int m = 0; m < 32; ++m) r[m] = pack_bf16x2(piece(2 * m), piece(2 * m + 1));
+            } else if (kt < p.ktw) {
                 const uint32_t s0 = sb[0] * 0x10001u, b0 = sb[1] * 0x10001u;  // bf16x2 broadcast
                 const uint32_t s1 = sb[2] * 0x10001u, b1 = sb[3] * 0x10001u;
                 // The packed rows arrive 32-byte (Q4) / 64-byte (Q8) swizzled: 16-byte chunk h of
@@ -612,6 +697,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                  const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_t,
                  const Params p) {
     qgemm_body<BITS, SWIGLU, CG, false>(tm_x, tm_w, tm_w2, tm_t, p, Gated{});
+}
+
+// f32 / f16 activations through the three-pass bf16 split (1-CTA tiles, plain or GELU).
+template <int BITS>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    qgemm_x3_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                    const Params p) {
+    qgemm_body<BITS, false, 1, false, false, true>(tm_x, tm_w, tm_w, tm_x, p, Gated{});
 }
 
 // Plain or gated linear plus a LoKr delta (1-CTA tiles, no SwiGLU).
@@ -847,6 +940,99 @@ int launch_qgemm_sm100(const void *x, int64_t M, int64_t K, const uint32_t *wq, 
     if (bits == 4)
         return swiglu ? launch_g<4, true, 1>(mx, mw, mw2, mt, p, gd, max_ctas, st) : launch_g<4, false, 1>(mx, mw, mw2, mt, p, gd, max_ctas, st);
     return swiglu ? launch_g<8, true, 1>(mx, mw, mw2, mt, p, gd, max_ctas, st) : launch_g<8, false, 1>(mx, mw, mw2, mt, p, gd, max_ctas, st);
+}
+
+}  // namespace ql
+
+namespace ql {
+namespace gemm {
+
+// x (f32 or f16) [M, K] -> the two bf16 pieces [M, 2 * Kp]: hi = bf16(x) at column k, lo =
+// bf16(x - hi) at column Kp + k; columns K..Kp-1 of both halves are zero.
+__global__ void split_x_kernel(const void *__restrict__ x, int x_dtype, int64_t M, int64_t K, int64_t Kp,
+                               __nv_bfloat16 *__restrict__ xs) {
+    const int64_t total = M * Kp;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / Kp, k = i - m * Kp;
+        const float v = k < K ? load_as_f32(x, x_dtype, m * K + k) : 0.f;
+        const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+        xs[m * 2 * Kp + k] = hi;
+        xs[m * 2 * Kp + Kp + k] = __float2bfloat16_rn(v - __bfloat162float(hi));
+    }
+}
+
+}  // namespace gemm
+
+size_t qgemm_x3_workspace(int64_t M, int64_t K) {
+    const int64_t Kp = (K + gemm::BK - 1) / gemm::BK * gemm::BK;
+    return (size_t)M * (size_t)Kp * 2 * 2;
+}
+
+// y [M, N] (f32 or f16) = x [M, K] (f32 or f16) . dequant(W)^T (+ bias, GELU) on tcgen05
+// tensor cores: x and each dequantized weight are split into two bf16 pieces and three
+// bf16 passes (whi.xhi + whi.xlo + wlo.xhi) accumulate in fp32.  Each piece pair keeps 16
+// significant bits, so a product is exact to about 2^-16 of |w x| (the dropped wlo.xlo term
+// and the pieces' roundings) and the sum carries the fp32 accumulation error on top.
+int launch_qgemm_x3(const void *x, int x_dtype, int64_t M, int64_t K, const uint32_t *wq, const void *scales,
+                    const void *biases, int sb_dtype, int64_t N, int gs, int bits, const void *bias, int act,
+                    void *y, int y_dtype, void *workspace, int max_ctas, cudaStream_t st) {
+    using namespace gemm;
+    const int64_t Kp = (K + BK - 1) / BK * BK;
+    __nv_bfloat16 *xs = static_cast<__nv_bfloat16 *>(workspace);
+    {
+        int dev = 0, sms = 148;
+        QL_CUDA_TRY(cudaGetDevice(&dev));
+        QL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        const int64_t total = M * Kp;
+        int64_t blocks = (total + 255) / 256;
+        if (blocks > (int64_t)sms * 8) blocks = (int64_t)sms * 8;
+        split_x_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, x_dtype, M, K, Kp, xs);
+        QL_CUDA_TRY(cudaGetLastError());
+    }
+    Params p{};
+    p.M = (int)M;
+    p.N = (int)N;
+    p.K = (int)K;
+    p.gs = gs;
+    p.G = (int)(K / gs);
+    p.ktw = (int)(Kp / BK);
+    p.ktl = 0;
+    p.act = act | (y_dtype == QL_F32 ? QL_EPI_OUT_F32 : QL_EPI_OUT_F16) | (sb_dtype == QL_F16 ? QL_EPI_SB_F16 : 0);
+    p.num_w_tiles = (int)((N + BW - 1) / BW);
+    p.num_t_tiles = (int)((M + BT - 1) / BT);
+    p.scales = (const __nv_bfloat16 *)scales;
+    p.biases = (const __nv_bfloat16 *)biases;
+    p.bias = (const __nv_bfloat16 *)bias;
+    p.y = (__nv_bfloat16 *)y;
+    CUtensorMap mx, mw;
+    int rc = make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xs, (uint64_t)(2 * Kp), (uint64_t)M,
+                         (uint64_t)(2 * Kp) * 2, BK, BT, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    const uint64_t words = (uint64_t)K * bits / 32;
+    rc = make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wq, words, (uint64_t)N, words * 4,
+                     (uint32_t)(BK * bits / 32), BW, bits == 4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+    auto kfn = bits == 4 ? qgemm_x3_kernel<4> : qgemm_x3_kernel<8>;
+    const int smem_bytes = bits == 4 ? Cfg<4, 1>::SMEM_TOTAL : Cfg<8, 1>::SMEM_TOTAL;
+    static PerDeviceFlag configured4, configured8;
+    PerDeviceFlag &configured = bits == 4 ? configured4 : configured8;
+    int dev = 0, sms = 148;
+    QL_CUDA_TRY(cudaGetDevice(&dev));
+    if (!configured.test(dev)) {
+        QL_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes));
+        configured.set(dev);
+    }
+    QL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int tiles = p.num_w_tiles * p.num_t_tiles;
+    int ctas = tiles < sms ? tiles : sms;
+    if (max_ctas > 0 && ctas > max_ctas) ctas = max_ctas;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ctas);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = smem_bytes;
+    cfg.stream = st;
+    QL_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, mx, mw, p));
+    return QL_OK;
 }
 
 }  // namespace ql

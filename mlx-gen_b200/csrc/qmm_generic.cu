@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(256) qmm_generic_kernel(const Params p) {
                     const uint32_t w = p.wq[ps][(int64_t)n * wpr + k / epw];
                     const uint32_t code = (w >> (p.bits * (k % epw))) & ((1u << p.bits) - 1u);
                     const int64_t g = (int64_t)n * p.G + k / p.gs;
-                    v = round_to(p.sdt, fmaf((float)code, load_as_f32(p.scales[ps], p.sdt, g),
+                    v = round_to(p.ydt, fmaf((float)code, load_as_f32(p.scales[ps], p.sdt, g),
                                              load_as_f32(p.biases[ps], p.sdt, g)));
                     if (p.lokr_delta && ps == 0)  // LoKr: w + scale * delta, in fp32
                         v = fmaf(p.lokr_scale, load_as_f32(p.lokr_delta, p.xdt, (int64_t)n * p.K + k), v);

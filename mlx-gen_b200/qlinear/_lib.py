@@ -42,6 +42,7 @@ EXPORTS = (
     "ql_matmul_workspace_size",
     "ql_quantized_matmul_noalloc",
     "ql_debug_inject",
+    "ql_matmul_workspace_size_x",
 )
 
 
@@ -107,6 +108,8 @@ def lib():
         L.ql_quantized_matmul_noalloc.argtypes = L.ql_quantized_matmul.argtypes
         L.ql_matmul_workspace_size.argtypes = [i64, i64, i64, C.POINTER(Epilogue)]
         L.ql_matmul_workspace_size.restype = C.c_size_t
+        L.ql_matmul_workspace_size_x.argtypes = [i64, i64, i64, C.POINTER(Epilogue), i32]
+        L.ql_matmul_workspace_size_x.restype = C.c_size_t
         for f in ("ql_quantize", "ql_dequantize", "ql_dequantize_rows", "ql_layernorm_modulate", "ql_quantized_matmul",
                   "ql_quantized_matmul_noalloc"):
             getattr(L, f).restype = i32

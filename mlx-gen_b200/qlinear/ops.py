@@ -197,6 +197,15 @@ def quantized_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, bi
         raise ValueError("a gate needs a residual")
     ep.kernel = kernel
     ep.max_ctas = max_ctas
+    if x2.dtype in (torch.float32, torch.float16) and lora is None:
+        # f32 / f16 activations: the workspace that lets them run on the tensor cores
+        need = int(lib().ql_matmul_workspace_size_x(M, N, K, C.byref(ep), dtype_code(x2)))
+        if need:
+            if workspace is None or workspace.numel() * workspace.element_size() < need:
+                workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+            keep.append(workspace)
+            ep.workspace = workspace.data_ptr()
+            ep.workspace_bytes = workspace.numel() * workspace.element_size()
     check(lib().ql_quantized_matmul(_ptr(x2), dtype_code(x2), M, K, _ptr(wq.contiguous()),
                                     _ptr(scales.contiguous()), _ptr(biases.contiguous()),
                                     dtype_code(scales), N, group_size, bits, 1, C.byref(ep), _ptr(y),

@@ -242,7 +242,10 @@ int qref_qmm(const void *x, int x_dtype, int64_t M, int64_t K, const uint32_t *w
         for (int64_t k = 0; k < K; ++k) {
             float s = load_el(scales, sb_dtype, n * G + k / gs);
             float b = load_el(biases, sb_dtype, n * G + k / gs);
-            deq[k] = round_to(sb_dtype, fmaf((float)code_at(wq + n * W, bits, k), s, b));
+            /* the dequantized weight in the computation dtype, promote(x, scales) = the
+               output dtype (mlx casts the operands of quantized_matmul to it): bf16 x with bf16
+               scales rounds w to bf16; f32 or mixed-dtype activations keep the fp32 value */
+            deq[k] = round_to(y_dtype, fmaf((float)code_at(wq + n * W, bits, k), s, b));
         }
         for (int64_t m = 0; m < M; ++m) {
             double acc = 0;
