@@ -440,6 +440,51 @@ def other_configs(dev, iters=5):
 
     ms = timed(zimage)
     fl = 2 * M * (4 * D * D + 2 * F * D + D * F)
+    # FLUX.1 block linears with f32 activations (FLUX.2 / Qwen image streams feed f32 x):
+    # the tensor-core three-pass split path, f32 output
+    M, h, f = 4608, 3072, 12288
+    fl_lin = [(qlin(3 * h, h, 8), h, 3 * h, None), (qlin(h, h, 8), h, h, None),
+              (qlin(f, h, 8), h, f, "gelu_tanh"), (qlin(h, f, 8), f, h, None)]
+    xs32 = {k: torch.randn(M, k, device=dev, generator=g) for k in (h, f)}
+    ys32 = {n: torch.empty(M, n, device=dev) for n in (h, 3 * h, f)}
+    wsx = torch.empty(max(int(qlinear.ops.lib().ql_matmul_workspace_size_x(M, 1, k, None, 0)) for k in (h, f)),
+                      dtype=torch.uint8, device=dev)
+
+    def flux_f32():
+        for w_, k, n, a in fl_lin:
+            qlinear.quantized_matmul(xs32[k], *w_, True, 64, 8, act=a, out=ys32[n], workspace=wsx)
+
+    ms32 = timed(flux_f32)
+    fl32 = sum(2 * M * n * k for _, k, n, _ in fl_lin)
+    out["flux_q8_block_f32_activations"] = {"value": fl32 / (ms32 * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms32,
+                                            "path": "tcgen05 GEMM, three bf16 passes (x and w split hi + lo)"}
+    del fl_lin, xs32, ys32, wsx
+    # adaLN prologue (FLUX's layer_norm + modulate before the QKV and MLP-up linears) as its
+    # own one-pass kernel: its cost against the linears it feeds
+    xm = torch.randn(M, h, device=dev, generator=g).to(torch.bfloat16)
+    sc = (torch.randn(h, device=dev, generator=g) * 0.1).to(torch.bfloat16)
+    sh = (torch.randn(h, device=dev, generator=g) * 0.1).to(torch.bfloat16)
+    wqkv, wup = qlin(3 * h, h, 8), qlin(f, h, 8)
+    yq = torch.empty(M, 3 * h, device=dev, dtype=torch.bfloat16)
+    yu = torch.empty(M, f, device=dev, dtype=torch.bfloat16)
+    xn = qlinear.layernorm_modulate(xm, sc, sh)
+
+    def gemms_only():
+        qlinear.quantized_matmul(xn, *wqkv, True, 64, 8, out=yq)
+        qlinear.quantized_matmul(xn, *wup, True, 64, 8, act="gelu_tanh", out=yu)
+
+    def with_adaln():
+        x1 = qlinear.layernorm_modulate(xm, sc, sh)
+        qlinear.quantized_matmul(x1, *wqkv, True, 64, 8, out=yq)
+        x2 = qlinear.layernorm_modulate(xm, sc, sh)
+        qlinear.quantized_matmul(x2, *wup, True, 64, 8, act="gelu_tanh", out=yu)
+
+    t_g, t_a = timed(gemms_only), timed(with_adaln)
+    out["adaln_prologue_overhead"] = {"gemms_ms": t_g, "with_two_adaln_passes_ms": t_a,
+                                      "overhead_frac": (t_a - t_g) / t_g,
+                                      "shape": "FLUX Q8 QKV 3072->9216 and MLP-up 3072->12288 at M=4608, each fed "
+                                               "by its own layer_norm + modulate pass over x [4608, 3072] bf16"}
+    del xm, yq, yu, xn
     out["zimage_q4_lora32_block"] = {"value": fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms,
                                      "lora_gflop_not_counted": 2 * M * 32 * (5 * D + 4 * D + F) / 1e9}
     return out

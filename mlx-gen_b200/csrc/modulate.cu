@@ -81,12 +81,95 @@ __global__ void __launch_bounds__(THREADS) ln_modulate_kernel(const __nv_bfloat1
     }
 }
 
+// The same computation with the row held in registers: each thread loads its 16-byte
+// chunks of x (and of scale / shift) once, so x is read from HBM exactly once and the two
+// statistics passes and the output pass run on registers.  D a multiple of 8, D <= 8 * 256 * MAXC.
+constexpr int MAXC = 4;
+template <bool F32_OUT>
+__global__ void __launch_bounds__(THREADS) ln_modulate_reg_kernel(const __nv_bfloat16 *__restrict__ x, int D, float eps,
+                                                                  const __nv_bfloat16 *__restrict__ scale,
+                                                                  const __nv_bfloat16 *__restrict__ shift,
+                                                                  int64_t period, void *__restrict__ y) {
+    __shared__ float red[THREADS / 32];
+    const int64_t m = blockIdx.x;
+    const int nch = D / 8;
+    uint4 xv[MAXC];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < MAXC; ++j) {
+        const int c = threadIdx.x + j * THREADS;
+        xv[j] = c < nch ? __ldg(reinterpret_cast<const uint4 *>(x + m * D) + c) : make_uint4(0, 0, 0, 0);
+        const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s += bf16lo(w[i]) + bf16hi(w[i]);
+    }
+    const float mean = block_sum(s, red) / (float)D;
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < MAXC; ++j) {
+        if (threadIdx.x + j * THREADS >= nch) continue;
+        const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float a = bf16lo(w[i]) - mean, b = bf16hi(w[i]) - mean;
+            q += a * a + b * b;
+        }
+    }
+    const float var = block_sum(q, red) / (float)D;
+    const float inv = 1.0f / sqrtf(var + eps);
+    const int64_t gr = period > 0 ? m / period : 0;
+#pragma unroll
+    for (int j = 0; j < MAXC; ++j) {
+        const int c = threadIdx.x + j * THREADS;
+        if (c >= nch) continue;
+        const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+        uint4 scv = make_uint4(0, 0, 0, 0), shv = scv;
+        if (scale) scv = __ldg(reinterpret_cast<const uint4 *>(scale + gr * D) + c);
+        if (shift) shv = __ldg(reinterpret_cast<const uint4 *>(shift + gr * D) + c);
+        const uint32_t sw[4] = {scv.x, scv.y, scv.z, scv.w}, hw[4] = {shv.x, shv.y, shv.z, shv.w};
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float v = (i & 1) ? bf16hi(w[i >> 1]) : bf16lo(w[i >> 1]);
+            float r = round_bf16((v - mean) * inv);
+            if (scale) {
+                const float s1 = ((i & 1) ? bf16hi(sw[i >> 1]) : bf16lo(sw[i >> 1])) + 1.0f;
+                r = F32_OUT ? r * s1 : round_bf16(r * round_bf16(s1));
+            }
+            if (shift) r = r + ((i & 1) ? bf16hi(hw[i >> 1]) : bf16lo(hw[i >> 1]));
+            o[i] = r;
+        }
+        if (F32_OUT) {
+            float4 *yp = reinterpret_cast<float4 *>(reinterpret_cast<float *>(y) + m * D) + 2 * c;
+            yp[0] = make_float4(o[0], o[1], o[2], o[3]);
+            yp[1] = make_float4(o[4], o[5], o[6], o[7]);
+        } else {
+            reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(y) + m * D)[c] =
+                make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                           pack_bf16x2(o[6], o[7]));
+        }
+    }
+}
+
 }  // namespace modulate_k
 
 int launch_ln_modulate(const void *x, int64_t M, int64_t D, float eps, const void *scale, const void *shift,
                        int64_t period, void *y, int y_dtype, cudaStream_t st) {
     if (M <= 0) return QL_OK;
     const dim3 grid((unsigned)M);
+    const bool al = ((reinterpret_cast<uintptr_t>(scale) | reinterpret_cast<uintptr_t>(shift)) & 15) == 0;
+    if (D <= 8 * modulate_k::THREADS * modulate_k::MAXC && al) {
+        if (y_dtype == QL_F32)
+            modulate_k::ln_modulate_reg_kernel<true><<<grid, modulate_k::THREADS, 0, st>>>(
+                (const __nv_bfloat16 *)x, (int)D, eps, (const __nv_bfloat16 *)scale, (const __nv_bfloat16 *)shift,
+                period, y);
+        else
+            modulate_k::ln_modulate_reg_kernel<false><<<grid, modulate_k::THREADS, 0, st>>>(
+                (const __nv_bfloat16 *)x, (int)D, eps, (const __nv_bfloat16 *)scale, (const __nv_bfloat16 *)shift,
+                period, y);
+        QL_CUDA_TRY(cudaGetLastError());
+        return QL_OK;
+    }
     if (y_dtype == QL_F32)
         modulate_k::ln_modulate_kernel<true><<<grid, modulate_k::THREADS, 0, st>>>(
             (const __nv_bfloat16 *)x, (int)D, eps, (const __nv_bfloat16 *)scale, (const __nv_bfloat16 *)shift, period, y);
