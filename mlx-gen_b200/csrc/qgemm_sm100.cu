@@ -619,7 +619,8 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                     // 32768 + c (one prmt).  s * (32768 + c) is exact in fp32 (8 x 16
                     // significant bits), so fma(s, 32768 + c, b - 32768 s) is the fp32
                     // rounding of s c + b whenever b - 32768 s is exact -- the same value
-                    // as fma(c, s, b) -- and within an fp32 ulp of 32768 s otherwise.
+                    // as fma(c, s, b) -- and within an fp32 ulp of 32768 s otherwise.  Two codes
+                    // per fma.rn.f32x2.
                     const float fs0 = bf16lo(s0), fs1 = bf16lo(s1);
                     const float fb0 = fmaf(-32768.f, fs0, bf16lo(b0)), fb1 = fmaf(-32768.f, fs1, bf16lo(b1));
 #pragma unroll
@@ -630,12 +631,17 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                         for (int i = 0; i < 4; ++i) {
                             const int wi = 4 * h + i;  // word index: codes 4wi..4wi+3
                             const float ss = wi < 8 ? fs0 : fs1, bb = wi < 8 ? fb0 : fb1;
-                            const float c0 = fmaf(__uint_as_float(prmt(wv[i], 0x47000000u, 0x7604u)), ss, bb);
-                            const float c1 = fmaf(__uint_as_float(prmt(wv[i], 0x47000000u, 0x7614u)), ss, bb);
-                            const float c2 = fmaf(__uint_as_float(prmt(wv[i], 0x47000000u, 0x7624u)), ss, bb);
-                            const float c3 = fmaf(__uint_as_float(prmt(wv[i], 0x47000000u, 0x7634u)), ss, bb);
-                            r[2 * wi] = pack_bf16x2(c0, c1);
-                            r[2 * wi + 1] = pack_bf16x2(c2, c3);
+                            uint32_t lo0, hi0, lo1, hi1;
+                            asm("{\n\t.reg .b64 a, b, c, d;\n\t"
+                                "mov.b64 a, {%4, %5};\n\tmov.b64 b, {%8, %8};\n\tmov.b64 c, {%9, %9};\n\t"
+                                "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t"
+                                "mov.b64 a, {%6, %7};\n\tfma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%2, %3}, d;\n\t}"
+                                : "=r"(lo0), "=r"(hi0), "=r"(lo1), "=r"(hi1)
+                                : "r"(prmt(wv[i], 0x47000000u, 0x7604u)), "r"(prmt(wv[i], 0x47000000u, 0x7614u)),
+                                  "r"(prmt(wv[i], 0x47000000u, 0x7624u)), "r"(prmt(wv[i], 0x47000000u, 0x7634u)),
+                                  "r"(__float_as_uint(ss)), "r"(__float_as_uint(bb)));
+                            r[2 * wi] = pack_bf16x2(__uint_as_float(lo0), __uint_as_float(hi0));
+                            r[2 * wi + 1] = pack_bf16x2(__uint_as_float(lo1), __uint_as_float(hi1));
                         }
                     }
                 }
