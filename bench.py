@@ -611,7 +611,7 @@ def run_ours(args):
     M, gs, bits = cfg["M"], cfg["gs"], cfg["bits"]
 
     # weights: generated and quantized identically on every rank, then sharded by qlinear.tp
-    blk, weights, x, ext, spec = build_block(cfg, flux_linears, dev, 0, comm, args.comm_sms, chunks=2)
+    blk, weights, x, ext, spec = build_block(cfg, flux_linears, dev, 0, comm, args.comm_sms, chunks=args.flux_chunks)
     # the TP output against the unsharded single-GPU block (before any timing)
     par = tp_parity(blk, weights, spec, cfg, x, ext)
     del weights
@@ -675,7 +675,7 @@ def run_ours(args):
                              "mlp": cfg["mlp"], "bits": bits, "group_size": gs,
                              "flops_per_step": total_flops,
                              "parallelism": f"tp{world}" if world > 1 else "single",
-                             "overlap": "row-parallel outputs all-reduced in 2 M-slices on a second stream, overlapping the next slice's GEMM; the consumer's slice i starts once slice i is reduced" if world > 1 else None,
+                             "overlap": f"row-parallel outputs all-reduced in {len(blk.bounds)} M-slices on a second stream, overlapping the next slice's GEMM; the consumer's slice i starts once slice i is reduced" if world > 1 else None,
                              "l2": "no flush: each step touches ~300 MB (> 126 MB L2)"},
                   "gpu_launches": blk.launches * args.steps,
                   "tp_parity": par,
@@ -770,7 +770,7 @@ def run_ours(args):
         del blk, x, xd2, yd2, x_alt
         torch.cuda.empty_cache()
         wcfg = dict(WAN)
-        wblk, wweights, wx, wext, wspec = build_block(wcfg, wan_linears, dev, 4, comm, args.comm_sms, chunks=4,
+        wblk, wweights, wx, wext, wspec = build_block(wcfg, wan_linears, dev, 4, comm, args.comm_sms, chunks=args.wan_chunks,
                                                       mode="seqpar")
         wpar = tp_parity(wblk, wweights, wspec, wcfg, wx, wext)
         del wweights
@@ -825,6 +825,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip cpu_baseline and decode_gemv")
     ap.add_argument("--comm-sms", type=int, default=8, help="SMs left to NCCL when N > 1")
+    ap.add_argument("--flux-chunks", type=int, default=2, help="token-row slices of the FLUX block's reductions")
+    ap.add_argument("--wan-chunks", type=int, default=4, help="token-row slices of the Wan block's reductions")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
