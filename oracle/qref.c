@@ -28,7 +28,15 @@
  *   - the per-element code uses a true division (w - bias) / scale;
  *   - for a bf16/f16 input the statistics, scale and bias are computed in fp32
  *     from the (exactly upcast) input; codes use the fp32 scale/bias; scale and
- *     bias are rounded to the storage dtype only when stored.
+ *     bias are rounded to the storage dtype only when stored.  This follows the
+ *     structure of MLX's published affine quantization (its CPU `quantize` and the
+ *     Metal `affine_quantize` kernel accumulate the group min/max and derive scale
+ *     and bias in float, quantize each element with those float values, and cast
+ *     scale/bias to the output dtype at the store); it is not pinned by a golden
+ *     vector of the reference for bf16 input.
+ *   - quantized_matmul dequantizes in the computation dtype promote(x, scales)
+ *     (mlx casts the operands to the result dtype): bf16 x with bf16 scales rounds
+ *     each weight to bf16, f32 or mixed-dtype activations keep the fp32 value.
  *
  * dtype codes: 0 = f32, 1 = bf16, 2 = f16  (same numbering as include/qlinear.h).
  */
