@@ -1,7 +1,7 @@
 """ctypes binding of libqlinear.so (the C ABI declared in include/qlinear.h).
 
 This is the Python counterpart of the Rust FFI crate a reference-side
-maintainer would add: raw `extern "C"` signatures, no
+maintainer would add (`qlinear-sys`): raw `extern "C"` signatures, no
 logic.  Loading fails loudly when the library has not been built -- there is
 no CPU or PyTorch fallback behind it.
 """
