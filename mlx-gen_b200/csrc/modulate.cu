@@ -30,6 +30,19 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
     return t;
 }
 
+// the same over a block of any whole number of warps (red holds 32 floats)
+__device__ __forceinline__ float block_sum_n(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int w = 0; w < nw; ++w) t += red[w];
+    return t;
+}
+
 // one CTA per row; rows of a few KB stay in L1 between the passes
 template <bool F32_OUT>
 __global__ void __launch_bounds__(THREADS) ln_modulate_kernel(const __nv_bfloat16 *__restrict__ x, int D, float eps,
@@ -81,33 +94,37 @@ __global__ void __launch_bounds__(THREADS) ln_modulate_kernel(const __nv_bfloat1
     }
 }
 
-// The same computation with the row held in registers: each thread loads its 16-byte
+// The same computation with the row held in registers: each thread loads its MAXC 16-byte
 // chunks of x (and of scale / shift) once, so x is read from HBM exactly once and the two
-// statistics passes and the output pass run on registers.  D a multiple of 8, D <= 8 * 256 * MAXC.
+// statistics passes and the output pass run on registers.  The block is sized to the row
+// (ceil(D / 8 / MAXC) threads rounded up to a warp, D a multiple of 8, D <= 8 * 1024 *
+// MAXC), so that short rows (FLUX's 3072: 96 threads) leave room for many rows in flight
+// on each SM -- one 256-thread block per row held too few bytes in flight per SM to
+// cover HBM latency.
 constexpr int MAXC = 4;
 template <bool F32_OUT>
-__global__ void __launch_bounds__(THREADS) ln_modulate_reg_kernel(const __nv_bfloat16 *__restrict__ x, int D, float eps,
+__global__ void __launch_bounds__(1024) ln_modulate_reg_kernel(const __nv_bfloat16 *__restrict__ x, int D, float eps,
                                                                   const __nv_bfloat16 *__restrict__ scale,
                                                                   const __nv_bfloat16 *__restrict__ shift,
                                                                   int64_t period, void *__restrict__ y) {
-    __shared__ float red[THREADS / 32];
+    __shared__ float red[32];
     const int64_t m = blockIdx.x;
-    const int nch = D / 8;
+    const int nch = D / 8, nt = blockDim.x;
     uint4 xv[MAXC];
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < MAXC; ++j) {
-        const int c = threadIdx.x + j * THREADS;
+        const int c = threadIdx.x + j * nt;
         xv[j] = c < nch ? __ldg(reinterpret_cast<const uint4 *>(x + m * D) + c) : make_uint4(0, 0, 0, 0);
         const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) s += bf16lo(w[i]) + bf16hi(w[i]);
     }
-    const float mean = block_sum(s, red) / (float)D;
+    const float mean = block_sum_n(s, red) / (float)D;
     float q = 0.f;
 #pragma unroll
     for (int j = 0; j < MAXC; ++j) {
-        if (threadIdx.x + j * THREADS >= nch) continue;
+        if (threadIdx.x + j * nt >= nch) continue;
         const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -115,12 +132,12 @@ __global__ void __launch_bounds__(THREADS) ln_modulate_reg_kernel(const __nv_bfl
             q += a * a + b * b;
         }
     }
-    const float var = block_sum(q, red) / (float)D;
+    const float var = block_sum_n(q, red) / (float)D;
     const float inv = 1.0f / sqrtf(var + eps);
     const int64_t gr = period > 0 ? m / period : 0;
 #pragma unroll
     for (int j = 0; j < MAXC; ++j) {
-        const int c = threadIdx.x + j * THREADS;
+        const int c = threadIdx.x + j * nt;
         if (c >= nch) continue;
         const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
         uint4 scv = make_uint4(0, 0, 0, 0), shv = scv;
@@ -158,13 +175,14 @@ int launch_ln_modulate(const void *x, int64_t M, int64_t D, float eps, const voi
     if (M <= 0) return QL_OK;
     const dim3 grid((unsigned)M);
     const bool al = ((reinterpret_cast<uintptr_t>(scale) | reinterpret_cast<uintptr_t>(shift)) & 15) == 0;
-    if (D <= 8 * modulate_k::THREADS * modulate_k::MAXC && al) {
+    if (D <= 8 * 1024 * modulate_k::MAXC && al) {
+        const int nt = (int)((((D / 8 + modulate_k::MAXC - 1) / modulate_k::MAXC) + 31) / 32 * 32);
         if (y_dtype == QL_F32)
-            modulate_k::ln_modulate_reg_kernel<true><<<grid, modulate_k::THREADS, 0, st>>>(
+            modulate_k::ln_modulate_reg_kernel<true><<<grid, nt, 0, st>>>(
                 (const __nv_bfloat16 *)x, (int)D, eps, (const __nv_bfloat16 *)scale, (const __nv_bfloat16 *)shift,
                 period, y);
         else
-            modulate_k::ln_modulate_reg_kernel<false><<<grid, modulate_k::THREADS, 0, st>>>(
+            modulate_k::ln_modulate_reg_kernel<false><<<grid, nt, 0, st>>>(
                 (const __nv_bfloat16 *)x, (int)D, eps, (const __nv_bfloat16 *)scale, (const __nv_bfloat16 *)shift,
                 period, y);
         QL_CUDA_TRY(cudaGetLastError());
