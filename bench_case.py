@@ -1,10 +1,11 @@
 """One quantized_matmul shape, timed with CUDA events (also the small case used for ncu
 captures).  Usage:
 
-    python bench_case.py M N K BITS [ACT|none] [REPS] [KERNEL]
+    python bench_case.py M N K BITS [ACT|none] [REPS] [KERNEL] [LORA_RANK]
 
 ACT: none, gelu_tanh, gelu or swiglu (a second W of the same shape as the up projection).
 KERNEL: auto, gemm, gemm2, gemv, gemv_tc, gemv_tma, gemv_regs or generic.
+LORA_RANK: r > 0 adds a LoRA adapter (A [K, r], B [r, N] ~N(0, 0.02), scale 0.5), fused.
 
 Prints time per call and TFLOP/s / GB/s.
 Weights ~N(0, 0.02) bf16 quantized on the device (group 64), x ~N(0, 1), bias ~N(0, 0.02).
@@ -40,9 +41,16 @@ def main(argv):
         up = qlinear.quantize(w3, 64, bits)
         del w3
     y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    rank = int(argv[7]) if len(argv) > 7 else 0
+    lora = None
+    if rank > 0:
+        la = (torch.randn(K, rank, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        lb = (torch.randn(rank, N, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        lora = (la, lb, 0.5)
 
     def f():
-        qlinear.quantized_matmul(x, wq, s, b, True, 64, bits, bias=bias, act=act, up=up, kernel=kernel, out=y)
+        qlinear.quantized_matmul(x, wq, s, b, True, 64, bits, bias=bias, act=act, up=up, kernel=kernel, out=y,
+                                 lora=lora)
 
     for _ in range(3):
         f()
@@ -56,7 +64,7 @@ def main(argv):
     ms = e0.elapsed_time(e1) / reps
     npass = 2 if act == "swiglu" else 1
     nbytes = npass * (N * K * bits // 8 + N * (K // 64) * 4) + (M * K + M * N) * 2
-    print(f"M={M} N={N} K={K} Q{bits} act={act}: {ms * 1e3:.1f} us  {2 * npass * M * N * K / ms / 1e9:.1f} TFLOP/s  "
+    print(f"M={M} N={N} K={K} Q{bits} act={act}{f' lora={rank}' if rank else ''}: {ms * 1e3:.1f} us  {2 * npass * M * N * K / ms / 1e9:.1f} TFLOP/s  "
           f"{nbytes / ms / 1e6:.1f} GB/s")
 
 

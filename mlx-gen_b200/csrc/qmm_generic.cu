@@ -120,11 +120,17 @@ __global__ void __launch_bounds__(256) qmm_generic_kernel(const Params p) {
 
 // LoRA pre-pass on tensor cores: T[M, rpad] = bf16(scale * (x . A)), columns >= rank zero.
 // x [M, K] bf16 (read once, the cost of this pass), A [K, rank] bf16 (small, L2-resident).
-// CTA tile 32 rows x 64 columns of T, 4 warps of 16 x 32; K in chunks of 64 through a
-// 8-deep cp.async ring of 128-byte rows with a 16-byte-unit XOR swizzle (conflict-free
-// ldmatrix); mma.sync.m16n8k16 bf16 with fp32 accumulation.
+// CTA tile 32 rows x 64 columns of T; K in chunks of 64 through an 8-deep ring of 128-byte
+// rows with a 16-byte-unit XOR swizzle (conflict-free ldmatrix); mma.sync.m16n8k16 bf16
+// with fp32 accumulation.  Eight warps: warps w and w + 4 own the same 16 x 32 piece of
+// the tile and take the first / second half of each chunk's K, so that each warp's chain
+// of dependent MMAs per chunk is half as long; their partials meet in shared memory at the
+// end.  KS = 2: the CTAs of a 2-CTA cluster take the two halves of the chunk range and the
+// second pushes its partial tile into the first's shared memory (distributed shared
+// memory), which doubles the CTAs (and the warps per SM) when the row tiles alone do not
+// fill the GPU.
 namespace lt {
-constexpr int BM = 32, BN = 64, BKC = 64, ST = 8;
+constexpr int BM = 32, BN = 64, BKC = 64, ST = 8, NT = 256;
 constexpr int SMEM = ST * (BM + BKC) * 128 + 1024;
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src, int src_bytes) {
@@ -161,26 +167,30 @@ __device__ __forceinline__ int swz(int r, int c) { return r * 128 + ((c ^ (r & 7
 // every thread issues 16-byte cp.async copies (A's rank not a multiple of 8).
 // NH = 16-column halves per warp: 2 computes all 64 columns of the tile, 1 only the first
 // 32 (rank <= 32) and writes zeros to the rest.
-template <bool TMA, int NH>
-__global__ void __launch_bounds__(128) lora_t_mma_kernel(const __grid_constant__ CUtensorMap tm_x,
-                                                          const __grid_constant__ CUtensorMap tm_a,
-                                                          const __nv_bfloat16 *__restrict__ x, int M, int K,
-                                                          const __nv_bfloat16 *__restrict__ A, int rank, int rpad,
-                                                          float scale, __nv_bfloat16 *__restrict__ T, int vec_a) {
+template <bool TMA, int NH, int KS>
+__global__ void __launch_bounds__(NT) lora_t_mma_kernel(const __grid_constant__ CUtensorMap tm_x,
+                                                         const __grid_constant__ CUtensorMap tm_a,
+                                                         const __nv_bfloat16 *__restrict__ x, int M, int K,
+                                                         const __nv_bfloat16 *__restrict__ A, int rank, int rpad,
+                                                         float scale, __nv_bfloat16 *__restrict__ T, int vec_a) {
     extern __shared__ uint8_t lt_smem_raw[];
     __shared__ uint64_t full[ST];
     __shared__ int abort_flag;
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(lt_smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t(*sx)[BM * 128] = reinterpret_cast<uint8_t(*)[BM * 128]>(base);
     uint8_t(*sa)[BKC * 128] = reinterpret_cast<uint8_t(*)[BKC * 128]>(base + ST * BM * 128);
-    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int kr = KS > 1 ? (int)cluster_ctarank() : 0;  // this CTA's part of K
+    const int mt = blockIdx.x / KS;
+    const int m0 = mt * BM, n0 = blockIdx.y * BN;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int wm = warp & 1, wn = warp >> 1;  // rows 16 wm .. +16, columns 16 NH wn .. + 16 NH
-    const int nk = (K + BKC - 1) / BKC;
+    const int tp = warp & 3, kh = warp >> 2;  // piece of the tile, half of each chunk's K
+    const int wm = tp & 1, wn = tp >> 1;      // rows 16 wm .. +16, columns 16 NH wn .. + 16 NH
+    const int nk_all = (K + BKC - 1) / BKC;
+    const int c0 = kr * nk_all / KS, nk = (kr + 1) * nk_all / KS - c0;  // this CTA's chunks
 
     // CTAs start at different K chunks so that they do not all read the same lines of A
     // at once (144 CTAs on one L2 line serialise); each CTA still sums its chunks in order
-    const int kstart = (int)((blockIdx.x * 5u) % (unsigned)nk);
+    const int kstart = nk > 0 ? (int)((mt * 5u) % (unsigned)nk) : 0;
     if (TMA) {
         if (tid == 0) {
             for (int i = 0; i < ST; ++i) mbar_init(&full[i], 1);
@@ -190,36 +200,38 @@ __global__ void __launch_bounds__(128) lora_t_mma_kernel(const __grid_constant__
         __syncthreads();
     }
     auto load = [&](int kc, int s) {
-        int kr = kc + kstart;
-        if (kr >= nk) kr -= nk;
-        const int k0 = kr * BKC;
-        if (TMA) {
+        int kq = kc + kstart;
+        if (kq >= nk) kq -= nk;
+        const int k0 = (c0 + kq) * BKC;
+        if constexpr (TMA) {
             if (tid == 0) {
                 mbar_arrive_expect_tx(&full[s], (BM + BKC) * 128);
                 tma_load_2d(sx[s], &tm_x, &full[s], k0, m0);
                 tma_load_2d(sa[s], &tm_a, &full[s], n0, k0);
             }
-            return;
-        }
-        for (int i = tid; i < BM * 8; i += 128) {
-            const int r = i >> 3, c = i & 7, m = m0 + r, k = k0 + c * 8;
-            const bool ok = m < M && k < K;  // K is a multiple of 8
-            cp_async16(sx[s] + swz(r, c), ok ? (const void *)(x + (int64_t)m * K + k) : (const void *)x, ok ? 16 : 0);
-        }
-        for (int i = tid; i < BKC * 8; i += 128) {
-            const int r = i >> 3, c = i & 7, k = k0 + r, n = n0 + c * 8;
-            if (vec_a) {
-                const bool ok = k < K && n < rank;  // rank is a multiple of 8 here
-                cp_async16(sa[s] + swz(r, c), ok ? (const void *)(A + (int64_t)k * rank + n) : (const void *)A,
+        } else {
+            for (int i = tid; i < BM * 8; i += NT) {
+                const int r = i >> 3, c = i & 7, m = m0 + r, k = k0 + c * 8;
+                const bool ok = m < M && k < K;  // K is a multiple of 8
+                cp_async16(sx[s] + swz(r, c), ok ? (const void *)(x + (int64_t)m * K + k) : (const void *)x,
                            ok ? 16 : 0);
-            } else {
-                uint16_t v[8];
+            }
+            for (int i = tid; i < BKC * 8; i += NT) {
+                const int r = i >> 3, c = i & 7, k = k0 + r, n = n0 + c * 8;
+                if (vec_a) {
+                    const bool ok = k < K && n < rank;  // rank is a multiple of 8 here
+                    cp_async16(sa[s] + swz(r, c), ok ? (const void *)(A + (int64_t)k * rank + n) : (const void *)A,
+                               ok ? 16 : 0);
+                } else {
+                    uint16_t v[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    v[e] = (k < K && n + e < rank) ? reinterpret_cast<const uint16_t *>(A)[(int64_t)k * rank + n + e] : 0;
-                *reinterpret_cast<uint4 *>(sa[s] + swz(r, c)) =
-                    make_uint4(v[0] | (uint32_t)v[1] << 16, v[2] | (uint32_t)v[3] << 16, v[4] | (uint32_t)v[5] << 16,
-                               v[6] | (uint32_t)v[7] << 16);
+                    for (int e = 0; e < 8; ++e)
+                        v[e] = (k < K && n + e < rank) ? reinterpret_cast<const uint16_t *>(A)[(int64_t)k * rank + n + e]
+                                                       : 0;
+                    *reinterpret_cast<uint4 *>(sa[s] + swz(r, c)) =
+                        make_uint4(v[0] | (uint32_t)v[1] << 16, v[2] | (uint32_t)v[3] << 16,
+                                   v[4] | (uint32_t)v[5] << 16, v[6] | (uint32_t)v[7] << 16);
+                }
             }
         }
     };
@@ -241,7 +253,8 @@ __global__ void __launch_bounds__(128) lora_t_mma_kernel(const __grid_constant__
         const int s = kc % ST;
         const uint32_t xb = smem_u32(sx[s]), ab = smem_u32(sa[s]);
 #pragma unroll
-        for (int kk = 0; kk < BKC / 16; ++kk) {
+        for (int k2 = 0; k2 < BKC / 32; ++k2) {
+            const int kk = 2 * kh + k2;
             uint32_t af[4];
             ldsm_x4(xb + swz(16 * wm + (lane & 15), 2 * kk + (lane >> 4)), af);
 #pragma unroll
@@ -254,6 +267,49 @@ __global__ void __launch_bounds__(128) lora_t_mma_kernel(const __grid_constant__
         }
     }
     cp_async_wait<0>();
+    __syncthreads();  // every chunk consumed: the ring's memory is reused below
+
+    // partials: [tp][lane][8 NH floats]; the upper half of the warps hands its K half to the
+    // lower half, then (KS = 2) the second CTA of the cluster hands its tile to the first
+    constexpr int RED = 4 * 32 * 8 * NH;  // floats
+    float *red = reinterpret_cast<float *>(base);
+    float *peer = red + RED;
+    float *mine = red + (tp * 32 + lane) * 8 * NH;
+    if (kh == 1) {
+#pragma unroll
+        for (int j = 0; j < 2 * NH; ++j)
+            *reinterpret_cast<float4 *>(mine + 4 * j) = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+    }
+    __syncthreads();
+    if (kh == 0) {
+#pragma unroll
+        for (int j = 0; j < 2 * NH; ++j) {
+            const float4 v = *reinterpret_cast<const float4 *>(mine + 4 * j);
+            acc[j][0] += v.x, acc[j][1] += v.y, acc[j][2] += v.z, acc[j][3] += v.w;
+        }
+    }
+    if constexpr (KS > 1) {
+        cluster_sync_all();  // both CTAs are past their ring and their first reduction
+        if (kr == 1 && kh == 0) {
+            const uint32_t dst = mapa_shared(smem_u32(peer + (tp * 32 + lane) * 8 * NH), 0);
+#pragma unroll
+            for (int j = 0; j < 2 * NH; ++j)
+                asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst + 16 * j), "f"(acc[j][0]),
+                             "f"(acc[j][1]), "f"(acc[j][2]), "f"(acc[j][3])
+                             : "memory");
+        }
+        cluster_sync_all();  // the second CTA's partial is in the first's shared memory
+        if (kr == 1) return;
+        if (kh == 0) {
+            const float *pp = peer + (tp * 32 + lane) * 8 * NH;
+#pragma unroll
+            for (int j = 0; j < 2 * NH; ++j) {
+                const float4 v = *reinterpret_cast<const float4 *>(pp + 4 * j);
+                acc[j][0] += v.x, acc[j][1] += v.y, acc[j][2] += v.z, acc[j][3] += v.w;
+            }
+        }
+    }
+    if (kh != 0) return;
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
     for (int j = 0; j < 2 * NH; ++j) {
@@ -319,15 +375,20 @@ int launch_lora_t(const void *x, int64_t M, int64_t K, const void *A, int64_t ra
     const int rpad = (int)((rank + 63) / 64 * 64);
     using namespace generic::lt;
     const int vec_a = rank % 8 == 0 && reinterpret_cast<uintptr_t>(A) % 16 == 0;
-    const dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)(rpad / BN));
-    static PerDeviceFlag configured;
+    static PerDeviceInt sm_count;
     const int cur_dev = current_device();
-    if (!configured.test(cur_dev)) {
-        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-        configured.set(cur_dev);
+    int sms = sm_count.get(cur_dev);
+    if (!sms) {
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cur_dev) != cudaSuccess || sms <= 0) sms = 148;
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<true, 1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<true, 2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<false, 1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<false, 2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<true, 1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<true, 2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<false, 1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        QL_CUDA_TRY(cudaFuncSetAttribute(lora_t_mma_kernel<false, 2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        sm_count.put(cur_dev, sms);
     }
     CUtensorMap mx{}, ma{};
     if (vec_a) {
@@ -337,16 +398,34 @@ int launch_lora_t(const void *x, int64_t M, int64_t K, const void *A, int64_t ra
         if (int rc = gemm::make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, (uint64_t)rank, (uint64_t)K,
                                        (uint64_t)rank * 2, BN, BKC, CU_TENSOR_MAP_SWIZZLE_128B))
             return rc;
-        auto kfn = rank <= 32 ? lora_t_mma_kernel<true, 1> : lora_t_mma_kernel<true, 2>;
-        kfn<<<grid, 128, SMEM, st>>>(mx, ma, (const __nv_bfloat16 *)x, (int)M, (int)K,
-                                                         (const __nv_bfloat16 *)A, (int)rank, rpad, scale,
-                                                         (__nv_bfloat16 *)T, vec_a);
-    } else {
-        auto kfn = rank <= 32 ? lora_t_mma_kernel<false, 1> : lora_t_mma_kernel<false, 2>;
-        kfn<<<grid, 128, SMEM, st>>>(mx, ma, (const __nv_bfloat16 *)x, (int)M, (int)K,
-                                                          (const __nv_bfloat16 *)A, (int)rank, rpad, scale,
-                                                          (__nv_bfloat16 *)T, vec_a);
     }
+    // two CTAs per row tile (K halves, cluster reduction) while the row tiles alone leave
+    // SMs without a second CTA; each CTA keeps at least two chunks
+    const int64_t tiles = ((M + BM - 1) / BM) * (rpad / BN);
+    const int ks = (tiles < 2 * (int64_t)sms && (K + BKC - 1) / BKC >= 4) ? 2 : 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((M + BM - 1) / BM * ks), (unsigned)(rpad / BN));
+    cfg.blockDim = dim3(NT);
+    cfg.dynamicSmemBytes = SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)ks;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const bool nh1 = rank <= 32;
+    void (*kfn)(CUtensorMap, CUtensorMap, const __nv_bfloat16 *, int, int, const __nv_bfloat16 *, int, int, float,
+                __nv_bfloat16 *, int);
+    if (vec_a)
+        kfn = ks == 2 ? (nh1 ? lora_t_mma_kernel<true, 1, 2> : lora_t_mma_kernel<true, 2, 2>)
+                      : (nh1 ? lora_t_mma_kernel<true, 1, 1> : lora_t_mma_kernel<true, 2, 1>);
+    else
+        kfn = ks == 2 ? (nh1 ? lora_t_mma_kernel<false, 1, 2> : lora_t_mma_kernel<false, 2, 2>)
+                      : (nh1 ? lora_t_mma_kernel<false, 1, 1> : lora_t_mma_kernel<false, 2, 1>);
+    QL_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, mx, ma, (const __nv_bfloat16 *)x, (int)M, (int)K,
+                                   (const __nv_bfloat16 *)A, (int)rank, rpad, scale, (__nv_bfloat16 *)T, vec_a));
     QL_CUDA_TRY(cudaGetLastError());
     return QL_OK;
 }
