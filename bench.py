@@ -600,6 +600,8 @@ def run_ours(args):
     if world > 1:
         # NCCL's log (e.g. its version banner) goes to stderr: stdout carries only the JSON line
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        if args.nccl_channels > 0:  # NCCL's CTAs per collective: the SMs the GEMMs leave free
+            os.environ.setdefault("NCCL_MAX_NCHANNELS", str(args.nccl_channels))
         # anything native code prints on fd 1 (NCCL's version banner) goes to stderr too;
         # the JSON line is written to the saved stdout
         sys.stdout.flush()
@@ -811,6 +813,9 @@ def run_ours(args):
                 result["decode_gemv"][f"M{m}"] = {"value": d["value"], "unit": "GB/s", "ms_per_step": d["ms_per_step"],
                                                   "frac_of_hbm": d["value"] / peaks["hbm_gbs"]}
             result["other_configs"] = other_configs(dev)
+            ad = result["other_configs"].get("adaln_prologue_overhead")
+            if ad:  # the two passes against the whole FLUX block step measured above
+                ad["frac_of_block_step"] = (ad["with_two_adaln_passes_ms"] - ad["gemms_ms"]) / result["ms_per_step"]
             result["quant_dequant"] = quant_dequant(dev, peaks)
         print(json.dumps(result), file=json_out, flush=True)
     if comm is not None:
@@ -825,6 +830,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip cpu_baseline and decode_gemv")
     ap.add_argument("--comm-sms", type=int, default=8, help="SMs left to NCCL when N > 1")
+    ap.add_argument("--nccl-channels", type=int, default=0,
+                    help="NCCL_MAX_NCHANNELS for N > 1 (0: NCCL's choice)")
     ap.add_argument("--flux-chunks", type=int, default=2, help="token-row slices of the FLUX block's reductions")
     ap.add_argument("--wan-chunks", type=int, default=4, help="token-row slices of the Wan block's reductions")
     args = ap.parse_args()
