@@ -583,6 +583,34 @@ def breakdown(blk, x, ext, steps, world):
             "note": f"rank {blk.rank}; separate {steps}-step run with events around every GEMM / collective"}
 
 
+def bind_host_to_gpu(dev):
+    """Pin this process to the CPUs NVML reports as closest to `dev` (read-only NVML query),
+    so that its pinned host buffers are allocated on the GPU's own NUMA node: with several
+    ranks copying at once, buffers on one socket made the host side the bottleneck.
+    Returns the number of CPUs bound to, or None when NVML cannot say."""
+    try:
+        import pynvml
+        import torch
+
+        pr = torch.cuda.get_device_properties(dev)
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:"
+                                                     f"{pr.pci_device_id:02x}.0".encode())
+            nwords = (os.cpu_count() + 63) // 64
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, nwords)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (w >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return len(cpus)
+    except Exception:  # no NVML or no affinity information: leave the process unbound
+        return None
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -596,6 +624,7 @@ def run_ours(args):
     json_out = sys.stdout
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    host_cpus = bind_host_to_gpu(dev) if world > 1 else None
     comm = None
     if world > 1:
         # NCCL's log (e.g. its version banner) goes to stderr: stdout carries only the JSON line
@@ -800,7 +829,8 @@ def run_ours(args):
                                  "double-buffered on two copy streams under the neighbouring steps' GEMMs; "
                                  "two inputs alternate, the last 4 steps' outputs checked"
                                  + ("; each rank copies 1/N of the rows each way, x all-gathered over NCCL"
-                                    if world > 1 else "")}
+                                    if world > 1 else ""),
+                         "host_cpus_bound": host_cpus}
         if world == 1 and not args.no_extras:
             result["cpu_baseline"] = cpu_baseline_sample(cfg)
             result["decode_gemv"] = decode_gemv(dev)

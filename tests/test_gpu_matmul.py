@@ -112,6 +112,25 @@ def test_lora_epilogue(dev, kernel, rank):
     assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), ulps=4, atol_frac=2 ** -7, what=f"lora r{rank}")
 
 
+@pytest.mark.parametrize("M,K,rank", [(9600, 192, 8), (9600, 448, 40), (300, 192, 12), (300, 448, 12),
+                                       (300, 448, 40), (2304, 3840, 32)])
+def test_lora_prepass_splits(dev, M, K, rank):
+    """The LoRA pre-pass T = s.(x.A) in each of its forms: one CTA per row tile (many tiles,
+    or K under four chunks) and a 2-CTA cluster splitting the chunks with a DSMEM reduction
+    (odd chunk counts split unevenly), TMA-fed (rank % 8 == 0) and cp.async-fed, 32 or 64
+    columns computed; checked through the GEMM's output against the oracle."""
+    N, gs, bits = 256, 64, 4
+    rng, x, wq, s, b, xt, wqt, st, bt = make_case(dev, M, N, K, gs, bits, 1000 + rank + K)
+    A = rand_bf16((K, rank), 1.0 / np.sqrt(rank), rng)
+    B = rand_bf16((rank, N), 0.01, rng)
+    y = qlinear.quantized_matmul(xt, wqt, st, bt, True, gs, bits, lora=(np2t(A, dev), np2t(B, dev), 0.5),
+                                 kernel=GEMM)
+    torch.cuda.synchronize()
+    assert qlinear.device_error() == 0
+    ref = O.quantized_matmul(x, wq, s, b, gs, bits, lora_a=A, lora_b=B, lora_scale=0.5)
+    assert_bf16_close(O.to_f32(t2np(y)), O.to_f32(ref), ulps=4, atol_frac=2 ** -7, what=f"lora M{M} K{K} r{rank}")
+
+
 def test_kernels_agree_with_each_other(dev):
     """GEMM, GEMV (M<=8 slices) and the generic kernel on the same operands."""
     M, N, K, gs, bits = 8, 512, 1024, 64, 4
