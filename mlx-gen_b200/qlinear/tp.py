@@ -303,10 +303,11 @@ class TPBlock:
         return (self.shard[last], self.M // self.world) if last in self.shard else (self.out[last], self.M)
 
     def forward(self, x: torch.Tensor, inputs: Optional[Dict[str, torch.Tensor]] = None, evs=None,
-                cevs=None) -> torch.Tensor:
+                cevs=None, ev_names=None) -> torch.Tensor:
         """Runs the block on this rank; returns ``result_rows()[0]``.  `evs` / `cevs`, if
         lists, receive ``(name, start_event, end_event)`` for every GEMM launch (main
-        stream) / every slice's collectives (communication stream)."""
+        stream; only the linears in `ev_names` when given) / every slice's collectives
+        (communication stream)."""
         inputs = inputs or {}
         W = self.world
         ready = {}  # name -> per-slice events: rows r0:r1 of the (reduced) output are usable
@@ -324,11 +325,12 @@ class TPBlock:
             for c, (r0, r1) in enumerate(self.bounds if sliced else [(0, self.M)]):
                 if from_red and self.cuda:
                     self.main.wait_event(ready[src][c])  # rows r0:r1 of the input are reduced
-                if evs is not None and self.cuda:
+                rec = evs is not None and self.cuda and (ev_names is None or name in ev_names)
+                if rec:
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record()
                 self.matmul(inp[r0:r1], l, y[r0:r1], self.max_ctas)
-                if evs is not None and self.cuda:
+                if rec:
                     e1.record()
                     evs.append((name, e0, e1))
                 if name in self.reduced:
