@@ -532,23 +532,28 @@ def tp_parity(blk, weights, spec, cfg, x, ext):
     return tp.parity(got, ref, blk.world)
 
 
-def time_block(blk, inp, steps, warmup, world):
-    """Device time per step of `blk` (CUDA events, max over ranks)."""
+def time_block(blk, inp, steps, warmup, world, graph=False):
+    """Device time per step of `blk` (CUDA events, max over ranks); `graph`: each step is
+    one replay of the block captured as a CUDA graph."""
     import torch
     import torch.distributed as dist
 
+    gr = blk.capture(*inp) if graph else None
+    fwd = gr.replay if graph else (lambda: blk.forward(*inp))
     for _ in range(warmup):
-        blk.forward(*inp)
+        fwd()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(steps):
-        blk.forward(*inp)
+        fwd()
     t1.record()
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1) / steps
+    if gr is not None:
+        gr.reset()  # holds NCCL work: freed before the communicator's teardown
     if world > 1:
         tt = torch.tensor([ms], device=blk.dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -658,8 +663,25 @@ def run_ours(args):
     def step(record=False, xin=None, names=(ROOF,)):
         return blk.forward(x if xin is None else xin, ext, evs=evs if record else None, ev_names=set(names))
 
+    # --graph (N > 1): the device-timed step is issued as one CUDA graph replay of the
+    # sharded block (TPBlock.capture) instead of a dozen GEMM launches, collectives and
+    # stream joins from Python.  Measured equal at N = 2 and within run-to-run spread at
+    # N = 4, so eager stays the default.  N = 1 stays eager (its timed region records events
+    # around the MLP-up launch for the roofline); so does the e2e loop.
+    graphs = {}
+
+    def gstep(xin=None):
+        xin = x if xin is None else xin
+        key = xin.data_ptr()
+        if key not in graphs:
+            graphs[key] = blk.capture(xin, ext)
+        return graphs[key].replay()
+
+    use_graph = world > 1 and args.graph
+    run_step = gstep if use_graph else step
+
     for _ in range(max(args.warmup, 3)):
-        step()
+        run_step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -670,20 +692,23 @@ def run_ours(args):
     # same number of collectives)
     t_w = time.perf_counter()
     for _ in range(3):
-        step()
+        run_step()
     torch.cuda.synchronize()
     n_soak = torch.tensor([int(1.0 / max((time.perf_counter() - t_w) / 3, 1e-4))], device=dev)
     if world > 1:
         dist.all_reduce(n_soak, op=dist.ReduceOp.MAX)
     for _ in range(int(n_soak.item())):
-        step()
+        run_step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(args.steps):
-        step(record=(world == 1))
+        if use_graph:
+            gstep()
+        else:
+            step(record=(world == 1))
     t1.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -710,7 +735,7 @@ def run_ours(args):
                              "mlp": cfg["mlp"], "bits": bits, "group_size": gs,
                              "flops_per_step": total_flops,
                              "parallelism": f"tp{world}" if world > 1 else "single",
-                             "overlap": f"row-parallel outputs all-reduced in {len(blk.bounds)} M-slices on a second stream, overlapping the next slice's GEMM; the consumer's slice i starts once slice i is reduced" if world > 1 else None,
+                             "overlap": f"row-parallel outputs all-reduced in {len(blk.bounds)} M-slices on a second stream, overlapping the next slice's GEMM; the consumer's slice i starts once slice i is reduced" + ("; each step one CUDA graph replay" if use_graph else "") if world > 1 else None,
                              "l2": "no flush: each step touches ~300 MB (> 126 MB L2)"},
                   "gpu_launches": blk.launches * args.steps,
                   "tp_parity": par,
@@ -809,6 +834,9 @@ def run_ours(args):
         tt = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_ms = float(tt.item())
+    for gr in graphs.values():
+        gr.reset()  # the graphs hold NCCL work: freed before the communicator's teardown
+    graphs.clear()
     # the Wan2.2-shaped block: the multi-GPU scaling workload of the path, timed
     # at every N with the same tensor-parallel scheme
     wan = None
@@ -823,7 +851,7 @@ def run_ours(args):
         torch.cuda.empty_cache()
         if not wpar["ok"]:
             raise SystemExit(f"rank {rank}: tensor-parallel Wan block differs from the unsharded block: {wpar}")
-        wms = time_block(wblk, (wx, wext), steps=5, warmup=2, world=world)
+        wms = time_block(wblk, (wx, wext), steps=5, warmup=2, world=world, graph=world > 1 and args.graph)
         wbd = breakdown(wblk, wx, wext, 3, world) if world > 1 else None
         wan = {"workload": "wan2.2_q4_block_linears", "value": wblk.flops / (wms * 1e-3) / 1e12, "unit": "TFLOP/s",
                "ms_per_step": wms, "n_gpus": world, "M": WAN["M"], "flops_per_step": wblk.flops,
@@ -873,6 +901,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--graph", action="store_true", help="N > 1: time the sharded step as CUDA graph replays")
     ap.add_argument("--no-extras", action="store_true", help="skip cpu_baseline and decode_gemv")
     ap.add_argument("--comm-sms", type=int, default=8, help="SMs left to NCCL when N > 1")
     ap.add_argument("--nccl-channels", type=int, default=0,

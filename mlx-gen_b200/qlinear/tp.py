@@ -310,6 +310,8 @@ class TPBlock:
         (communication stream)."""
         inputs = inputs or {}
         W = self.world
+        if self.cuda:
+            self.main = torch.cuda.current_stream(self.dev)  # the caller's stream (a capture stream too)
         ready = {}  # name -> per-slice events: rows r0:r1 of the (reduced) output are usable
         for name, _, _, src in self.spec:
             l = self.lin[name]
@@ -338,6 +340,32 @@ class TPBlock:
         if self.comm_stream is not None:
             self.main.wait_stream(self.comm_stream)  # the block output's last slice is reduced
         return self.result_rows()[0]
+
+    def capture(self, x: torch.Tensor, inputs: Optional[Dict[str, torch.Tensor]] = None) -> "BlockGraph":
+        """``forward(x, inputs)`` captured into a CUDA graph: the GEMM launches, the
+        collectives (NCCL records them into the graph) and the stream joins between them.
+        A replay issues the whole block with one host call, so a short sharded step is not
+        bound by the host issuing dozens of launches.  x and the inputs are bound at capture:
+        fill those tensors, then replay.  Every rank must capture (and replay) the same
+        block in the same order, as with the eager forward.  The graph holds NCCL work of
+        the communicator: ``reset()`` every BlockGraph before ``Comm.close()``, whose
+        teardown otherwise waits on it."""
+        if not self.cuda:
+            raise ValueError("capture needs CUDA tensors")
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(side):
+            self.forward(x, inputs)  # warm-up on the capture's stream (communicators, caches)
+        torch.cuda.current_stream(self.dev).wait_stream(side)
+        torch.cuda.synchronize(self.dev)
+        pending = len(self.comm._pending) if self.comm is not None else 0
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            out = self.forward(x, inputs)
+        if self.comm is not None:
+            del self.comm._pending[pending:]  # capture-time handles: the replays carry no host work
+        self.main = torch.cuda.current_stream(self.dev)
+        return BlockGraph(g, out)
 
     def _reduce(self, name, y, r0, r1, cevs=None):
         W = self.world
@@ -389,6 +417,25 @@ class TPBlock:
             self.comm.all_gather(full[r0:r1], t[r0 // W:r1 // W].contiguous())
         self.comm.wait()
         return full
+
+
+class BlockGraph:
+    """A ``TPBlock.forward`` captured by ``TPBlock.capture``: ``replay()`` runs it on the
+    current stream and returns the block's output tensor (the same tensor every time)."""
+
+    def __init__(self, graph, out: torch.Tensor):
+        self.graph, self.out = graph, out
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.out
+
+    def reset(self) -> None:
+        """Synchronises and frees the graph (call before closing the communicator)."""
+        if self.graph is not None:
+            torch.cuda.synchronize(self.out.device)
+            self.graph.reset()
+            self.graph = None
 
 
 def reference_forward(spec, weights, group_size: int, bits: int, x: torch.Tensor,

@@ -52,7 +52,27 @@ def test_tp_block_single_gpu_is_the_unsharded_chain(dev, specname, bits):
     assert par["ok"] and par["bitwise_equal"]
 
 
-def _rank(rank, world, port, specname, mode, q):
+@pytest.mark.parametrize("specname,bits", [("flux", 8), ("wan", 4)])
+def test_tp_block_graph_replay_is_the_eager_forward(dev, specname, bits):
+    """TPBlock.capture: a CUDA-graph replay gives the eager forward's output bit for bit,
+    and a replay after the bound input changed follows the new input."""
+    from qlinear import tp
+    spec = FLUX_SPEC if specname == "flux" else WAN_SPEC
+    W, x, ext = _weights(dev, spec, 1024, 2048, bits, 3)
+    blk = tp.TPBlock(spec, W, 64, bits, x.shape[0], comm=None, device=dev)
+    want = blk.forward(x, ext).clone()
+    xb = x.clone()
+    gr = blk.capture(xb, ext)
+    assert torch.equal(gr.replay(), want)
+    x2 = torch.randn_like(x)
+    want2 = blk.forward(x2, ext).clone()
+    xb.copy_(x2)
+    got2 = gr.replay().clone()
+    torch.cuda.synchronize()
+    assert torch.equal(got2, want2)
+
+
+def _rank(rank, world, port, specname, mode, q, graph=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -63,8 +83,18 @@ def _rank(rank, world, port, specname, mode, q):
     W, x, ext = _weights(dev, spec, 1024, 2048, 8 if specname == "flux" else 4, 5)
     blk = tp.TPBlock(spec, W, 64, 8 if specname == "flux" else 4, x.shape[0], comm=comm, chunks=2, mode=mode,
                      device=dev)
-    blk.forward(x, ext)
+    if graph:
+        xb = x.clone()
+        gr = blk.capture(xb, ext)
+        xb.zero_()
+        gr.replay()
+        xb.copy_(x)  # the replay that counts reads the refilled input
+        gr.replay()
+    else:
+        blk.forward(x, ext)
     got = blk.gather_output()
+    if graph:
+        gr.reset()  # before the communicator's teardown
     ref = tp.reference_forward(spec, W, 64, 8 if specname == "flux" else 4, x, ext)["out"]
     torch.cuda.synchronize()
     q.put((rank, tp.parity(got, ref, world)))
@@ -72,12 +102,14 @@ def _rank(rank, world, port, specname, mode, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("specname,mode", [("flux", "allreduce"), ("wan", "seqpar")])
-def test_tp_block_two_gpus_matches_unsharded(specname, mode):
+@pytest.mark.parametrize("specname,mode,graph", [("flux", "allreduce", False), ("wan", "seqpar", False),
+                                                  ("flux", "allreduce", True), ("wan", "seqpar", True)])
+def test_tp_block_two_gpus_matches_unsharded(specname, mode, graph):
+    """NCCL ranks, eager and as a captured CUDA graph (collectives inside the graph)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29700 + os.getpid() % 200
-    ps = [ctx.Process(target=_rank, args=(r, 2, port, specname, mode, q)) for r in range(2)]
+    port = 29700 + (os.getpid() * 4 + 2 * graph + (mode == "seqpar")) % 200
+    ps = [ctx.Process(target=_rank, args=(r, 2, port, specname, mode, q, graph)) for r in range(2)]
     for p in ps:
         p.start()
     res = [q.get(timeout=300) for _ in ps]
