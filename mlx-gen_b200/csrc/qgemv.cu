@@ -308,9 +308,10 @@ int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const 
     static const bool env_regs = getenv("QL_GEMV_REGS") != nullptr;  // profiling switches
     const bool force_regs = env_regs || which == 2;
     static const bool force_mma = getenv("QL_GEMV_MMA") != nullptr;
-    // The tcgen05 kernel wins once its row tiles (128 rows, 64 with SwiGLU) fill the GPU,
-    // or at 6+ tokens (the mma.sync kernel's per-token folds grow with M); below that its
-    // fixed start-up (TMEM, activation conversion, pipeline fill) dominates.
+    // The tcgen05 kernel wins once its row tiles (128 rows, 64 with SwiGLU) fill the GPU;
+    // below that its fixed start-up (TMEM, activation conversion, pipeline fill) dominates
+    // at every M (Llama-3.2-3B decode step, per step: M = 6 1.85 ms on it against 1.56 on
+    // the register-fed kernel, M = 8 1.93 against 1.75 on the TMA-fed kernel).
     static PerDeviceInt sm_count;
     const int cur_dev = current_device();
     int n_sms = sm_count.get(cur_dev);
@@ -321,16 +322,19 @@ int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const 
     }
     static const bool force_tc = getenv("QL_GEMV_TC") != nullptr;
     const int64_t tiles = (N + (act == QL_ACT_SWIGLU ? 63 : 127)) / (act == QL_ACT_SWIGLU ? 64 : 128);
-    if (!force_regs && !force_mma && (force_tc || tiles >= n_sms || M >= 6) &&
+    if (!force_regs && !force_mma && (force_tc || tiles >= n_sms) &&
         qgemv_tc_supported(M, K, gs, bits, x, lora_t != nullptr) && all_aligned16({scales, biases, scales2, biases2}))
         return launch_qgemv_tc(x, M, K, wq, scales, biases, wq2, scales2, biases2, N, gs, bits, bias, bias2, act, y,
                                gd, st);
-    // Narrow projections at M = 1 and every shape at M = 2..5 run best on the register-fed
-    // kernel below (no TMA / barrier set-up; measured on the Llama-3.2-3B decode step).
-    const bool regs_pick = (M >= 2 && M <= 5) || (act != QL_ACT_SWIGLU && N <= 4096);
-    if (!force_regs && !regs_pick && qgemv_tma_supported(M, K, gs))
-        return launch_qgemv_tma(x, M, K, wq, scales, biases, wq2, scales2, biases2, N, gs, bits, bias, bias2, act,
-                                lora_t, lora_b, rank, y, gd, st);
+    // Narrow projections at M = 1 and every shape at M = 2..6 run best on the register-fed
+    // kernel below (no TMA / barrier set-up; measured on the Llama-3.2-3B decode step);
+    // wider ones at M = 1, 7, 8 on the TMA-fed one.
+    const bool regs_pick = (M >= 2 && M <= 6) || (act != QL_ACT_SWIGLU && N <= 4096);
+    if (!force_regs && !regs_pick && qgemv_tma_supported(M, K, gs)) {
+        const int rc = launch_qgemv_tma(x, M, K, wq, scales, biases, wq2, scales2, biases2, N, gs, bits, bias, bias2,
+                                        act, lora_t, lora_b, rank, y, gd, st);
+        if (rc != QL_EUNSUPPORTED) return rc;  // refused before launching: x does not fit its staging
+    }
     using namespace gemv;
     Params p{};
     p.gd = gd;
@@ -359,7 +363,14 @@ int launch_qgemv(const void *x, int64_t M, int64_t K, const uint32_t *wq, const 
     QL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int nstrips = (int)((N + 15) / 16);
     const size_t smem = (size_t)M * (size_t)((K + CHUNK - 1) / CHUNK * CHUNK + 32) * 2;
-    if (smem > 200 * 1024) return fail(QL_EUNSUPPORTED, "GEMV: M*K too large for the x staging buffer");
+    if (smem > 200 * 1024) {
+        // the tcgen05 kernel splits K over a cluster and may still take this x
+        if (!force_regs && qgemv_tc_supported(M, K, gs, bits, x, lora_t != nullptr) &&
+            all_aligned16({scales, biases, scales2, biases2}))
+            return launch_qgemv_tc(x, M, K, wq, scales, biases, wq2, scales2, biases2, N, gs, bits, bias, bias2, act,
+                                   y, gd, st);
+        return fail(QL_EUNSUPPORTED, "GEMV: M*K too large for the x staging buffer");
+    }
     const int per_sm = smem <= 48 * 1024 ? 2 : 1;
     const int grid = nstrips < per_sm * sms ? nstrips : per_sm * sms;
     const bool sw = act == QL_ACT_SWIGLU;
