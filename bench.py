@@ -735,7 +735,7 @@ def run_ours(args):
                              "mlp": cfg["mlp"], "bits": bits, "group_size": gs,
                              "flops_per_step": total_flops,
                              "parallelism": f"tp{world}" if world > 1 else "single",
-                             "overlap": f"row-parallel outputs all-reduced in {len(blk.bounds)} M-slices on a second stream, overlapping the next slice's GEMM; the consumer's slice i starts once slice i is reduced" + ("; each step one CUDA graph replay" if use_graph else "") if world > 1 else None,
+                             "overlap": (f"row-parallel outputs all-reduced in {len(blk.bounds)} M-slices on a second stream, overlapping the next slice's GEMM; the consumer's slice i starts once slice i is reduced" if len(blk.bounds) > 1 else "one all-reduce per row-parallel linear, no slicing") + ("; each step one CUDA graph replay" if use_graph else "") if world > 1 else None,
                              "l2": "no flush: each step touches ~300 MB (> 126 MB L2)"},
                   "gpu_launches": blk.launches * args.steps,
                   "tp_parity": par,
@@ -903,10 +903,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--graph", action="store_true", help="N > 1: time the sharded step as CUDA graph replays")
     ap.add_argument("--no-extras", action="store_true", help="skip cpu_baseline and decode_gemv")
-    ap.add_argument("--comm-sms", type=int, default=8, help="SMs left to NCCL when N > 1")
+    ap.add_argument("--comm-sms", type=int, default=0,
+                    help="SMs the GEMMs leave to NCCL when N > 1 (0 measured best at N = 4 and 8)")
     ap.add_argument("--nccl-channels", type=int, default=0,
                     help="NCCL_MAX_NCHANNELS for N > 1 (0: NCCL's choice)")
-    ap.add_argument("--flux-chunks", type=int, default=2, help="token-row slices of the FLUX block's reductions")
+    ap.add_argument("--flux-chunks", type=int, default=1,
+                    help="token-row slices of the FLUX block's reductions (1 measured best at N = 4 and 8)")
     ap.add_argument("--wan-chunks", type=int, default=4, help="token-row slices of the Wan block's reductions")
     args = ap.parse_args()
     if args.impl == "reference":

@@ -242,13 +242,15 @@ class TPBlock:
     input), the name of an external input passed to ``forward`` (full width; a row-parallel
     linear reads its K slice) or the name of an earlier linear.  weights: ``name ->
     (wq, scales, biases, bias)`` unsharded (identical on every rank).  comm: a ``Comm`` or
-    None (one process, unsharded).  The GEMMs leave `comm_sms` SMs to the collectives.
+    None (one process, unsharded).  The GEMMs leave `comm_sms` SMs to the collectives (0:
+    the GEMMs take every SM and NCCL's kernels share them -- measured fastest on the FLUX
+    and Wan blocks at 4 and 8 GPUs).
     `matmul(x, lin, out, max_ctas)` runs one linear (default: the C ABI's GEMM; tests
     substitute a CPU implementation)."""
 
     def __init__(self, spec: Sequence[Tuple[str, Optional[str], str, str]], weights: Dict[str, tuple],
                  group_size: int, bits: int, M: int, comm: Optional[Comm] = None, chunks: int = 2,
-                 mode: str = "allreduce", comm_sms: int = 8, dtype=torch.bfloat16,
+                 mode: str = "allreduce", comm_sms: int = 0, dtype=torch.bfloat16,
                  device: Optional[torch.device] = None,
                  matmul: Callable = default_matmul):
         if mode not in ("allreduce", "seqpar"):
