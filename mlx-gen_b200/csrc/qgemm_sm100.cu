@@ -404,6 +404,19 @@ __device__ __forceinline__ void qgemm_body(const CUtensorMap &tm_x, const CUtens
                         }
                     }
                     named_bar_sync(1, 128);
+                } else if (!GATED && n < p.N && p.act == QL_ACT_NONE && m0 + c * 32 + 32 <= p.M) {
+                    // plain linear, 32 tokens in range: the staged halves are the output bits
+                    // (short-K tiles are bound by this loop's instruction count)
+                    uint16_t *yp = reinterpret_cast<uint16_t *>(p.y) + (int64_t)(m0 + c * 32) * p.N + n;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        yp[(int64_t)i * p.N] = (uint16_t)((i & 1) ? (pk[i >> 1] >> 16) : pk[i >> 1]);
+                } else if (!GATED && n < p.N && p.act == QL_ACT_GELU_TANH && m0 + c * 32 + 32 <= p.M) {
+                    __nv_bfloat16 *yp = p.y + (int64_t)(m0 + c * 32) * p.N + n;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        yp[(int64_t)i * p.N] =
+                            __float2bfloat16_rn(gelu_tanh_f((i & 1) ? bf16hi(pk[i >> 1]) : bf16lo(pk[i >> 1])));
                 } else if (!GATED && n < p.N) {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
