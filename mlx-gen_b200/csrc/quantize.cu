@@ -111,7 +111,14 @@ __global__ void __launch_bounds__(256) quantize_kernel(const void *__restrict__ 
         // inside [-1, 300] the product is within 2^-13 of the quotient, so rint agrees
         // unless the product lies within 2^-10 of a rounding boundary (x.5); only then (or
         // for a NaN) is the exact division done.  The codes are the exact ones.
+        //
+        // rint without the slow rounding / conversion instructions: adding 1.5 * 2^23 rounds
+        // qf to an integer (round-to-nearest-even, exact for |qf| < 2^22) held in the low
+        // mantissa bits, so the sum's bit pattern minus that of 1.5 * 2^23 is rint(qf) as an
+        // integer.  The boundary test uses d = qf - rint(qf) (exact): qf lies within 2^-10 of
+        // x.5 exactly when |d| > 0.5 - 2^-10.
         const float rs = __frcp_rn(s);
+        constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
         uint32_t word[2] = {0u, 0u};
 #pragma unroll
         for (int h = 0; h < 2; ++h)
@@ -119,11 +126,17 @@ __global__ void __launch_bounds__(256) quantize_kernel(const void *__restrict__ 
             for (int i = 0; i < EPW; ++i) {
                 const float a = __fsub_rn(v[h][i], b);
                 float qf = __fmul_rn(a, rs);
-                const float fr = qf - floorf(qf);
+                float t = __fadd_rn(qf, kMagic);
+                const float d = __fsub_rn(qf, __fsub_rn(t, kMagic));
                 const bool in_range = qf >= -1.0f && qf <= 300.0f;
-                if ((in_range && fabsf(fr - 0.5f) < 0x1p-10f) || qf != qf) qf = __fdiv_rn(a, s);
-                float c = rintf(qf);
-                c = fminf(fmaxf(c, 0.0f), n_bins);
+                if ((in_range && fabsf(d) > 0.5f - 0x1p-10f) || qf != qf) {
+                    qf = __fdiv_rn(a, s);
+                    t = __fadd_rn(qf, kMagic);
+                }
+                // qf < 0 (and NaN) gives code 0, as the clamp of rint(qf) does; for qf >= 0 the
+                // sum is a positive float whose bits grow with qf
+                const int c =
+                    qf >= 0.0f ? min((int)(__float_as_uint(t) - __float_as_uint(kMagic)), (1 << BITS) - 1) : 0;
                 word[h] |= (uint32_t)c << (BITS * i);
             }
         reinterpret_cast<uint2 *>(wq)[t] = make_uint2(word[0], word[1]);
